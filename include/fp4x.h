@@ -1,0 +1,161 @@
+/*
+ * fp4x.h -- C ABI of the B200 (sm_100a) MXFP4 Llama decode hot path.
+ *
+ * Drop-in replacement for the operator API that botBehavior/rust-fp4-blackwell
+ * generates with cuda-oxide's #[cuda_module] (one typed launch method per
+ * #[kernel], examples/llama_run/src/main.rs:13-316, loaded at :488).  Each entry
+ * point below names the reference kernel (path:line) it replaces.  Differences
+ * from the reference boundary, all deliberate:
+ *   - the caller passes a cudaStream_t first and the LIBRARY chooses the launch
+ *     geometry (the reference's LaunchConfig, llama_run/src/main.rs:392-397, is
+ *     dropped);
+ *   - every call validates its arguments and returns an fp4x_status without
+ *     launching anything on failure (the reference unwrap()s, :513-535);
+ *   - pointers are raw device pointers with explicit sizes; no call allocates
+ *     device memory on the per-token path.
+ *
+ * Thread safety: calls on distinct streams / distinct model handles may run
+ * concurrently; the last-error string is thread-local.
+ */
+#ifndef FP4X_H
+#define FP4X_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FP4X_API __attribute__((visibility("default")))
+#else
+#define FP4X_API
+#endif
+
+typedef struct CUstream_st *fp4x_stream_t; /* == cudaStream_t */
+
+typedef enum {
+    FP4X_OK = 0,
+    FP4X_EINVAL = 1,      /* bad shape / alignment / null pointer; nothing launched */
+    FP4X_ECUDA = 2,       /* a CUDA runtime call failed; see fp4x_last_error() */
+    FP4X_ETIMEOUT = 3,    /* a bounded device-side wait expired */
+    FP4X_ENOMEM = 4,      /* allocation failed (model creation only) */
+    FP4X_EUNSUPPORTED = 5 /* valid request this build does not serve */
+} fp4x_status;
+
+/* ------------------------------------------------------------ library */
+
+/* Message of the last failing call on this host thread ("" if none). */
+FP4X_API const char *fp4x_last_error(void);
+/* Library version string. */
+FP4X_API const char *fp4x_version(void);
+/* Synchronises `stream`, then reads and clears the device error word that
+ * kernels set when a bounded wait expires.  Returns FP4X_ETIMEOUT if set. */
+FP4X_API int fp4x_device_error(fp4x_stream_t stream, uint32_t *bits_out);
+
+/* ------------------------------------------------------------ formats */
+
+/* Quantise an f32 [n][k] matrix to MXFP4 (E2M1 nibbles, two per byte, low
+ * nibble = lower k; one E8M0 byte = 2^(floor(log2 amax) - 2) per 32-block),
+ * values to the nearest E2M1 level with ties to the smaller magnitude.
+ * Replaces quant_fp4, examples/llama_run/src/main.rs:334-376, with the E8M0
+ * scale rule of the native format.  k % 32 == 0. */
+FP4X_API int fp4_quantize_mxfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w,
+                       uint8_t *packed /* [n][k/2] */, uint8_t *scales /* [n][k/32] */);
+/* Reference-layout quantiser, llama_run/src/main.rs:334-376 exactly: f32 scale
+ * amax/6 (1.0 for an all-zero block), u32 words of 8 nibbles. */
+FP4X_API int fp4_quantize_ref(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w,
+                     uint32_t *packed /* [n][k/8] */, float *scales /* [n][k/32] */);
+/* Dequantise MXFP4 to f32 (E2M1 x E8M0, exact). */
+FP4X_API int fp4_dequantize_mxfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint8_t *packed,
+                         const uint8_t *scales, float *out /* [n][k] */);
+/* Seeded synthetic tensors (this library's generator: splitmix64 + Irwin-Hall(12)
+ * normal, bit-identical on host and device). */
+FP4X_API int fp4x_fill_normal_f32(fp4x_stream_t stream, uint64_t seed, uint64_t offset, float sigma, float *out,
+                         size_t n);
+FP4X_API int fp4x_fill_normal_bf16(fp4x_stream_t stream, uint64_t seed, uint64_t offset, float sigma,
+                          uint16_t *out, size_t n);
+/* Generate an [n][k] N(0, sigma) matrix from `seed` and quantise it to MXFP4 in
+ * one pass (the f32 matrix is never materialised). */
+FP4X_API int fp4x_init_mxfp4(fp4x_stream_t stream, uint64_t seed, float sigma, uint32_t n, uint32_t k,
+                    uint8_t *packed, uint8_t *scales);
+
+/* ------------------------------------------------------------ operators */
+
+/* y[n] = sum_k e2m1(W[n,k]) * 2^(S[n,k/32]-127) * x[k]   (fp32 accumulation)
+ * Native MXFP4 storage, bf16 activation.  Replaces fp4_gemv,
+ * examples/llama_run/src/main.rs:34-77 (also fp4_gemv/src/main.rs:32-92).
+ * k % 32 == 0, 32 <= k <= 16384, w 16-byte aligned. */
+FP4X_API int fp4_gemv(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint8_t *w /* [n][k/2] */,
+             const uint8_t *scales /* [n][k/32] E8M0 */, const uint16_t *x /* bf16 [k] */,
+             float *y /* [n] */);
+/* Same operator on the reference's own storage: u32 words of 8 nibbles, f32
+ * scales, f32 x -- argument-for-argument the reference kernel's signature
+ * (llama_run/src/main.rs:35), a literal drop-in for its Layer buffers (:378-390). */
+FP4X_API int fp4_gemv_ref(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint32_t *w /* [n][k/8] */,
+                 const float *scales /* [n][k/32] */, const float *x /* [k] */, float *y /* [n] */);
+/* Native MXFP4 storage with an f32 activation (the decode engine's form). */
+FP4X_API int fp4_gemv_f32x(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint8_t *w, const uint8_t *scales,
+                  const float *x, float *y);
+
+/* y = x * rsqrt(mean(x^2) + eps) * weight.  Replaces rmsnorm,
+ * llama_run/src/main.rs:79-116 (test llama_rmsnorm/src/main.rs:14-56). */
+FP4X_API int llama_rmsnorm(fp4x_stream_t stream, uint32_t dim, float eps, const float *x, const float *weight,
+                  float *y);
+/* In-place rotate-half RoPE on q [num_heads][head_dim] with cos/sin rows at
+ * cos_base (= pos * head_dim/2).  Replaces rope, llama_run/src/main.rs:118-138. */
+FP4X_API int llama_rope(fp4x_stream_t stream, uint32_t num_heads, uint32_t head_dim, uint32_t cos_base,
+               const float *cos_t, const float *sin_t, float *q);
+/* Fill RoPE tables [n_pos][head_dim/2]: freq_j = theta^(-2j/hd) and angle
+ * pos*freq_j in f64, cast to f32 (llama_run/src/main.rs:462-471); computed on
+ * the host and copied to `cos_t`/`sin_t` (device). */
+FP4X_API int llama_rope_tables(fp4x_stream_t stream, uint32_t n_pos, uint32_t head_dim, double theta, float *cos_t,
+                      float *sin_t);
+/* dst[off + i] = src[i], i < n.  Replaces copy_into, llama_run/src/main.rs:140-146. */
+FP4X_API int llama_copy_into(fp4x_stream_t stream, uint32_t n, uint32_t off, const float *src, float *dst);
+/* bf16 KV append: dst_bf16[off + i] = bf16(src[i]) (the native bf16 cache). */
+FP4X_API int llama_kv_append_bf16(fp4x_stream_t stream, uint32_t n, uint32_t off, const float *src, uint16_t *dst);
+/* out = g / (1 + exp(-g)) * u.  Replaces swiglu, llama_run/src/main.rs:244-252. */
+FP4X_API int llama_swiglu(fp4x_stream_t stream, uint32_t n, const float *gate, const float *up, float *out);
+/* x += y.  Replaces residual, llama_run/src/main.rs:254-261. */
+FP4X_API int llama_residual(fp4x_stream_t stream, uint32_t n, const float *y, float *x);
+/* out[0] = argmax(logits), ties to the lowest index.  Replaces argmax,
+ * llama_run/src/main.rs:263-315. */
+FP4X_API int llama_argmax(fp4x_stream_t stream, uint32_t n, const float *logits, uint32_t *out);
+
+/* Single-query GQA attention on the reference's f32 cache layout
+ * [seq][n_kv][64]: out[h] = softmax(q[h] . K^T / sqrt(64)) V over t < seq.
+ * Argument-for-argument attn_decode, llama_run/src/main.rs:149 (head_dim is the
+ * reference's compile-time HD = 64, :19); kernel body :148-242, test
+ * llama_attn_decode/src/main.rs:18-129.  Any seq >= 1 (the reference caps seq at
+ * its shared-memory MAXSEQ).  No workspace: one CTA per q head. */
+FP4X_API int llama_attn_decode(fp4x_stream_t stream, uint32_t n_heads, uint32_t n_kv_heads, uint32_t seq,
+                      const float *q, const float *kc, const float *vc, float *out);
+/* Same with head_dim in {64, 128} and split-KV over the sequence when a
+ * workspace of llama_attn_workspace_size() bytes is given (NULL: no split). */
+FP4X_API int llama_attn_decode_hd(fp4x_stream_t stream, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                         uint32_t seq, const float *q, const float *kc, const float *vc, float *out,
+                         void *workspace, size_t workspace_bytes);
+/* Bytes of split-KV partials the batched attention entry points use for this
+ * shape (0: no split needed). */
+FP4X_API size_t llama_attn_workspace_size(uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                                 uint32_t seq);
+/* Batched bf16 flash-decode: q [B][n_heads][hd] bf16,
+ * caches [B][max_seq][n_kv][hd] bf16 (the reference's per-sequence layout,
+ * llama_run/src/main.rs:388-389, stacked over the batch), out [B][n_heads][hd]
+ * bf16; softmax scale 1/sqrt(hd), causal at position seq-1. */
+FP4X_API int llama_attn_decode_bf16(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                           uint32_t head_dim, uint32_t seq, uint32_t max_seq, const uint16_t *q,
+                           const uint16_t *kc, const uint16_t *vc, uint16_t *out, void *workspace,
+                           size_t workspace_bytes);
+/* The decode engine's form: f32 q and out, bf16 caches. */
+FP4X_API int llama_attn_decode_f32q_bf16kv(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                                  uint32_t head_dim, uint32_t seq, uint32_t max_seq, const float *q,
+                                  const uint16_t *kc, const uint16_t *vc, float *out, void *workspace,
+                                  size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FP4X_H */

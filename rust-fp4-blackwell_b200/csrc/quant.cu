@@ -1,0 +1,211 @@
+// quant.cu -- MXFP4 quantisation, dequantisation and the seeded synthetic
+// initialiser, on the device.
+//
+// Quantiser semantics restate quant_fp4, examples/llama_run/src/main.rs:334-376:
+// per (row, 32-block) amax; nearest E2M1 level by a strict '<' scan over the
+// ascending level table (ties -> smaller magnitude); v < 0 sets the sign bit even
+// when the magnitude rounds to 0 (-0).  Every step is an exactly rounded f32
+// operation (division, subtraction, fabs, compare), so results are bit-identical
+// to the CPU loop.  The native variant takes the E8M0 scale
+// 2^(floor(log2 amax) - 2) from the float's exponent bits.
+#include "common.cuh"
+
+namespace fp4x {
+namespace quant {
+
+__device__ __forceinline__ uint32_t nearest_code(float v) {
+    // llama_run/src/main.rs:332,348-363
+    const float levels[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const float a = fabsf(v);
+    uint32_t bc = 0;
+    float bd = 3.40282347e+38f;
+#pragma unroll
+    for (uint32_t ci = 0; ci < 8; ++ci) {
+        const float d = fabsf(__fsub_rn(a, levels[ci]));
+        if (d < bd) {
+            bd = d;
+            bc = ci;
+        }
+    }
+    return bc | (v < 0.0f ? 8u : 0u);
+}
+
+__device__ __forceinline__ int floor_log2_bits(float a) {
+    const uint32_t u = __float_as_uint(a) & 0x7FFFFFFFu;
+    const int ef = (int)(u >> 23);
+    if (ef != 0) return ef - 127;
+    return (31 - __clz(u & 0x7FFFFFu)) - 149;  // subnormal
+}
+
+__device__ __forceinline__ uint32_t e8m0_from_amax(float amax) {
+    if (!(amax > 0.0f)) return 127u;
+    int e = floor_log2_bits(amax) - 2 + 127;
+    e = max(0, min(254, e));
+    return (uint32_t)e;
+}
+
+// Quantise 32 values (in registers) into 16 packed bytes + the E8M0 byte.
+__device__ __forceinline__ void quant_block_mxfp4(const float (&v)[32], uint4 &packed, uint8_t &sbyte) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint32_t e = e8m0_from_amax(amax);
+    const float scale = e8m0_to_f32(e);
+    uint32_t words[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) words[i / 8] |= nearest_code(__fdiv_rn(v[i], scale)) << ((i % 8) * 4);
+    packed = make_uint4(words[0], words[1], words[2], words[3]);
+    sbyte = (uint8_t)e;
+}
+
+// One thread per (row, 32-block).
+__global__ void quant_mxfp4_kernel(uint64_t nblocks, const float *__restrict__ w, uint8_t *__restrict__ packed,
+                                   uint8_t *__restrict__ scales) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    float v[32];
+    const float4 *src = reinterpret_cast<const float4 *>(w + blk * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = src[i];
+        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+    }
+    uint4 p;
+    uint8_t s;
+    quant_block_mxfp4(v, p, s);
+    reinterpret_cast<uint4 *>(packed)[blk] = p;
+    scales[blk] = s;
+}
+
+// llama_run/src/main.rs:339-365 exactly: scale = amax/6 (1.0 for a zero block).
+__global__ void quant_ref_kernel(uint64_t nblocks, const float *__restrict__ w, uint32_t *__restrict__ packed,
+                                 float *__restrict__ scales) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    const float *src = w + blk * 32;
+    float amax = 0.0f;
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(src[i]));
+    const float scale = amax > 0.0f ? __fdiv_rn(amax, 6.0f) : 1.0f;
+    scales[blk] = scale;
+    uint32_t words[4] = {0, 0, 0, 0};
+    for (int i = 0; i < 32; ++i) words[i / 8] |= nearest_code(__fdiv_rn(src[i], scale)) << ((i % 8) * 4);
+    for (int j = 0; j < 4; ++j) packed[blk * 4 + j] = words[j];
+}
+
+// Dequantise through the same hardware E2M1 -> f16x2 conversion the GEMV uses,
+// so a bit-exact dequant test also pins the GEMV's decode.
+__global__ void dequant_mxfp4_kernel(uint64_t nblocks, const uint8_t *__restrict__ packed,
+                                     const uint8_t *__restrict__ scales, float *__restrict__ out) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    const uint4 p = reinterpret_cast<const uint4 *>(packed)[blk];
+    const float s = e8m0_to_f32(scales[blk]);
+    const uint32_t words[4] = {p.x, p.y, p.z, p.w};
+    float4 *dst = reinterpret_cast<float4 *>(out + blk * 32);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t h[4];
+        decode_word_f16(words[j], h);
+        float f[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half2 hh = *reinterpret_cast<const __half2 *>(&h[q]);
+            f[2 * q] = __low2float(hh) * s;
+            f[2 * q + 1] = __high2float(hh) * s;
+        }
+        dst[2 * j] = make_float4(f[0], f[1], f[2], f[3]);
+        dst[2 * j + 1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+}
+
+__global__ void fill_normal_f32_kernel(uint64_t seed, uint64_t offset, float sigma, float *__restrict__ out,
+                                       uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = normal_draw(seed, offset + i, sigma);
+}
+
+__global__ void fill_normal_bf16_kernel(uint64_t seed, uint64_t offset, float sigma, uint16_t *__restrict__ out,
+                                        uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = f32_to_bf16_bits(normal_draw(seed, offset + i, sigma));
+}
+
+// Generate + quantise one 32-block per thread; element index = row*k + col.
+__global__ void init_mxfp4_kernel(uint64_t seed, float sigma, uint64_t nblocks, uint8_t *__restrict__ packed,
+                                  uint8_t *__restrict__ scales) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = normal_draw(seed, blk * 32 + i, sigma);
+    uint4 p;
+    uint8_t s;
+    quant_block_mxfp4(v, p, s);
+    reinterpret_cast<uint4 *>(packed)[blk] = p;
+    scales[blk] = s;
+}
+
+inline unsigned grid_for(uint64_t n, unsigned block) { return (unsigned)((n + block - 1) / block); }
+
+}  // namespace quant
+}  // namespace fp4x
+
+using namespace fp4x;
+
+extern "C" int fp4_quantize_mxfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w, uint8_t *packed,
+                                  uint8_t *scales) {
+    FP4X_REQUIRE(w && packed && scales, "fp4_quantize_mxfp4: null pointer");
+    FP4X_REQUIRE(k % 32 == 0 && k > 0 && n > 0, "fp4_quantize_mxfp4: k=%u must be a positive multiple of 32", k);
+    FP4X_REQUIRE(aligned16(w) && aligned16(packed), "fp4_quantize_mxfp4: w and packed must be 16-byte aligned");
+    const uint64_t nb = (uint64_t)n * (k / 32);
+    quant::quant_mxfp4_kernel<<<quant::grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(nb, w, packed, scales);
+    return check_launch("fp4_quantize_mxfp4");
+}
+
+extern "C" int fp4_quantize_ref(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w, uint32_t *packed,
+                                float *scales) {
+    FP4X_REQUIRE(w && packed && scales, "fp4_quantize_ref: null pointer");
+    FP4X_REQUIRE(k % 32 == 0 && k > 0 && n > 0, "fp4_quantize_ref: k=%u must be a positive multiple of 32", k);
+    const uint64_t nb = (uint64_t)n * (k / 32);
+    quant::quant_ref_kernel<<<quant::grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(nb, w, packed, scales);
+    return check_launch("fp4_quantize_ref");
+}
+
+extern "C" int fp4_dequantize_mxfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint8_t *packed,
+                                    const uint8_t *scales, float *out) {
+    FP4X_REQUIRE(out && packed && scales, "fp4_dequantize_mxfp4: null pointer");
+    FP4X_REQUIRE(k % 32 == 0 && k > 0 && n > 0, "fp4_dequantize_mxfp4: k=%u must be a positive multiple of 32", k);
+    FP4X_REQUIRE(aligned16(out) && aligned16(packed), "fp4_dequantize_mxfp4: out and packed must be 16-byte aligned");
+    const uint64_t nb = (uint64_t)n * (k / 32);
+    quant::dequant_mxfp4_kernel<<<quant::grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(nb, packed, scales, out);
+    return check_launch("fp4_dequantize_mxfp4");
+}
+
+extern "C" int fp4x_fill_normal_f32(fp4x_stream_t stream, uint64_t seed, uint64_t offset, float sigma, float *out,
+                                    size_t n) {
+    FP4X_REQUIRE(out || n == 0, "fp4x_fill_normal_f32: null pointer");
+    if (n == 0) return FP4X_OK;
+    const unsigned grid = (unsigned)std::min<uint64_t>(quant::grid_for(n, 256), 148u * 16u);
+    quant::fill_normal_f32_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(seed, offset, sigma, out, n);
+    return check_launch("fp4x_fill_normal_f32");
+}
+
+extern "C" int fp4x_fill_normal_bf16(fp4x_stream_t stream, uint64_t seed, uint64_t offset, float sigma,
+                                     uint16_t *out, size_t n) {
+    FP4X_REQUIRE(out || n == 0, "fp4x_fill_normal_bf16: null pointer");
+    if (n == 0) return FP4X_OK;
+    const unsigned grid = (unsigned)std::min<uint64_t>(quant::grid_for(n, 256), 148u * 16u);
+    quant::fill_normal_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(seed, offset, sigma, out, n);
+    return check_launch("fp4x_fill_normal_bf16");
+}
+
+extern "C" int fp4x_init_mxfp4(fp4x_stream_t stream, uint64_t seed, float sigma, uint32_t n, uint32_t k,
+                               uint8_t *packed, uint8_t *scales) {
+    FP4X_REQUIRE(packed && scales, "fp4x_init_mxfp4: null pointer");
+    FP4X_REQUIRE(k % 32 == 0 && k > 0 && n > 0, "fp4x_init_mxfp4: k=%u must be a positive multiple of 32", k);
+    FP4X_REQUIRE(aligned16(packed), "fp4x_init_mxfp4: packed must be 16-byte aligned");
+    const uint64_t nb = (uint64_t)n * (k / 32);
+    quant::init_mxfp4_kernel<<<quant::grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(seed, sigma, nb, packed,
+                                                                                         scales);
+    return check_launch("fp4x_init_mxfp4");
+}
