@@ -155,6 +155,58 @@ FP4X_API int llama_attn_decode_f32q_bf16kv(fp4x_stream_t stream, uint32_t batch,
                                   const uint16_t *kc, const uint16_t *vc, float *out, void *workspace,
                                   size_t workspace_bytes);
 
+/* ------------------------------------------------------------ decode engine */
+
+/* Model shape + synthetic-init seed.  The reference hard-codes these as consts
+ * (examples/llama_run/src/main.rs:318-330, llama_decode/src/main.rs:289-298). */
+typedef struct fp4x_llama_config {
+    uint32_t n_layers, dim, ffn, n_heads, n_kv_heads, head_dim, vocab, max_seq;
+    float rope_theta, eps;
+    uint64_t seed;     /* tensor seeds = splitmix64(seed, tensor id) */
+    uint32_t tp_rank;  /* tensor-parallel shard of this process (0 without TP) */
+    uint32_t tp_size;  /* 1 (or 0) without TP */
+} fp4x_llama_config;
+
+typedef struct fp4x_llama_model fp4x_llama_model;
+
+/* Allocate and random-initialise a model on the current device: every linear
+ * (including lm_head) N(0, 0.02) quantised to MXFP4 with the E8M0 rule,
+ * embeddings bf16 N(0, 0.02), norm weights ones, bf16 KV cache, RoPE tables;
+ * captures the per-token CUDA graph.  Replaces the model set-up of
+ * llama_run/src/main.rs:432-489 (real weights) / llama_decode/src/main.rs:367-426
+ * (random weights). */
+FP4X_API int llama_model_create(const fp4x_llama_config *cfg, fp4x_llama_model **out);
+FP4X_API int llama_model_destroy(fp4x_llama_model *m);
+/* Zero the KV cache. */
+FP4X_API int llama_model_reset(fp4x_llama_model *m, fp4x_stream_t stream);
+/* forward(tok, pos) -> next token, llama_run/src/main.rs:492-536: one token at
+ * `pos`, writes the argmax (ties to the lowest index) to *next_host and, when
+ * non-NULL, the logits [vocab] to logits_host.  Synchronous, as the reference's
+ * per-token to_host_vec (:535). */
+FP4X_API int llama_forward(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t token, uint32_t pos,
+                           uint32_t *next_host, float *logits_host);
+/* One token of the device-resident loop (decode_step, llama_decode/src/main.rs:428-477):
+ * consumes the device token/position left by the previous step, asynchronous. */
+FP4X_API int llama_decode_step(fp4x_llama_model *m, fp4x_stream_t stream);
+/* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-587, EOS
+ * ignored): prefill the prompt one position at a time, then n_gen tokens.
+ * prompt/out_ids are HOST arrays; *prefill_ms covers the n_prompt forwards (the
+ * last yields the first generated token), *decode_ms the remaining n_gen-1
+ * (the reference's timed tokens, :554-562). */
+FP4X_API int llama_generate(fp4x_llama_model *m, fp4x_stream_t stream, const uint32_t *prompt, uint32_t n_prompt,
+                            uint32_t n_gen, uint32_t *out_ids, float *prefill_ms, float *decode_ms);
+/* Copy one MXFP4 tensor of the model to host in canonical row order (tensor id
+ * 1 = lm_head, 16 + 8*layer + {0..6} = q,k,v,o,gate,up,down); n_out/k_out get
+ * its shape.  Test hook for parity with the oracle. */
+FP4X_API int llama_model_export_tensor(fp4x_llama_model *m, uint32_t tensor_id, uint8_t *packed_host,
+                                       uint8_t *scales_host, uint32_t *n_out, uint32_t *k_out);
+/* Copy the bf16 embedding table [vocab][dim] to host. */
+FP4X_API int llama_model_embedding(fp4x_llama_model *m, uint16_t *embed_host);
+/* Kernel launches in one token's CUDA graph. */
+FP4X_API uint32_t llama_model_kernels_per_token(const fp4x_llama_model *m);
+/* MXFP4 bytes (packed + scales) streamed per token (all linears incl. lm_head). */
+FP4X_API size_t llama_model_weight_bytes(const fp4x_llama_model *m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -308,6 +308,8 @@ class Model:
             pass
 
     def forward(self, token: int, pos: int):
+        if not (0 <= pos < self.cfg["max_seq"] and 0 <= token < self.cfg["vocab"]):
+            raise ValueError(f"position {pos} / token {token} outside the model")
         logits = np.empty(self.cfg["vocab"], np.float32)
         nxt = lib().orc_forward(self._h, token, pos, _p(logits, C.c_float))
         return int(nxt), logits

@@ -566,6 +566,7 @@ static void lin(orc_model *m, const qmat *w, const float *x, float *y) {
  * are rounded to bf16 when appended and widened when read. */
 uint32_t orc_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits) {
     const orc_config *c = &m->c;
+    if (pos >= c->max_seq || token >= c->vocab) return UINT32_MAX; /* nothing written */
     uint32_t hd = c->head_dim, half = hd / 2, nkv = c->n_kv_heads, nh = c->n_heads;
     uint32_t kvd = nkv * hd, seq = pos + 1;
     const uint16_t *er = m->embed + (size_t)token * c->dim;

@@ -131,7 +131,8 @@ const uint8_t *orc_model_packed(const orc_model *m, uint32_t tensor_id);
 const uint8_t *orc_model_scales(const orc_model *m, uint32_t tensor_id);
 const uint16_t *orc_model_embed(const orc_model *m);
 /* One token through the model at `pos` (llama_run/src/main.rs:509-535); writes
- * logits[vocab] and returns the argmax. */
+ * logits[vocab] and returns the argmax (UINT32_MAX, nothing written, if pos >=
+ * max_seq or token >= vocab). */
 uint32_t orc_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits);
 /* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-570), EOS ignored. */
 void orc_generate(orc_model *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen,

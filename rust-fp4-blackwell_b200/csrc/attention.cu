@@ -16,6 +16,7 @@
 // Bound: HBM.  Algorithmic bytes per call = 2 * B * seq * n_kv * hd * sizeof(kv)
 //   (+ q and out); flops = 4 * B * n_heads * seq * hd.
 #include "common.cuh"
+#include "attention.cuh"
 
 #include <algorithm>
 
@@ -64,15 +65,7 @@ __device__ __forceinline__ void load_chunk8(const uint16_t *p, float (&k)[8]) {
     }
 }
 
-struct Params {
-    uint32_t batch, n_heads, n_kv, seq, max_seq, splits, split_len;
-    float scale;
-    const void *q;   // [B][n_heads][hd]
-    const void *kc;  // [B][max_seq][n_kv][hd]
-    const void *vc;
-    void *out;       // [B][n_heads][hd]
-    float *ws;       // [B][n_heads][splits][hd + 2] partials (splits > 1)
-};
+
 
 // grid = (splits, n_heads / HPC, batch); HPC q heads (one KV head) per CTA.
 template <int HD, int HPC, typename QT, typename KT, typename OT>
@@ -84,11 +77,15 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
     __shared__ float wo[kWarps][HPC][HD];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t split = blockIdx.x, hgrp = blockIdx.y, b = blockIdx.z;
     constexpr uint32_t H = HPC;
     const uint32_t h0 = hgrp * H;
     const uint32_t group = p.n_heads / p.n_kv, kvh = h0 / group;
-    const uint32_t t_begin = split * p.split_len, t_end = min(p.seq, t_begin + p.split_len);
+    const uint32_t seq = p.pos_ptr ? *p.pos_ptr + 1 : p.seq;
+    const uint32_t t_begin = split * p.split_len, t_end = min(seq, t_begin + p.split_len);
+    if (t_begin >= seq) return;  // slice past the current position (whole CTA, before any barrier)
 
     const QT *q = reinterpret_cast<const QT *>(p.q) + ((size_t)b * p.n_heads + h0) * HD;
     for (uint32_t i = tid; i < H * HD; i += kThreads) qs[i / HD][i % HD] = to_f32(q[i]) * p.scale;
@@ -197,10 +194,13 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
 // grid = (n_heads, batch), block = HD: merge the slices of one (b, head).
 template <int HD, typename OT>
 __global__ void attn_combine_kernel(Params p) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const size_t bh = (size_t)b * p.n_heads + h;
     const float *rec = p.ws + bh * p.splits * (HD + 2);
-    const uint32_t used = (p.seq + p.split_len - 1) / p.split_len;
+    const uint32_t seq = p.pos_ptr ? *p.pos_ptr + 1 : p.seq;
+    const uint32_t used = (seq + p.split_len - 1) / p.split_len;
     float M = -INFINITY;
     for (uint32_t s = 0; s < used; ++s) M = fmaxf(M, rec[s * (HD + 2)]);
     float L = 0.0f, O = 0.0f;
@@ -255,6 +255,7 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
     p.splits = (seq + p.split_len - 1) / p.split_len;
     p.scale = 1.0f / sqrtf((float)hd);
     p.q = q, p.kc = kc, p.vc = vc, p.out = out, p.ws = static_cast<float *>(ws);
+    p.pos_ptr = nullptr;
     dim3 grid(p.splits, n_heads / hpc, batch);
 #define FP4X_ATTN_CASE(HD_, HPC_)                                                                       \
     if (hd == HD_ && hpc == HPC_) {                                                                   \
@@ -269,6 +270,46 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
     FP4X_ATTN_CASE(128, 8)
 #undef FP4X_ATTN_CASE
     return check_launch("llama_attn_decode");
+}
+
+// Engine form: f32 q/out, bf16 caches, seq from *pos_ptr + 1 on the device, a
+// fixed grid of `splits` slices of `split_len` tokens (slices past seq exit),
+// launched with programmatic dependent launch.
+template <int HD, int HPC>
+int launch_engine_t(cudaStream_t stream, const Params &p, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.splits, p.n_heads / HPC, p.batch);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_split_kernel<HD, HPC, float, uint16_t, float>, p);
+    if (e == cudaSuccess && p.splits > 1) {
+        cudaLaunchConfig_t c2 = cfg;
+        c2.gridDim = dim3(p.n_heads, p.batch);
+        c2.blockDim = dim3(HD);
+        e = cudaLaunchKernelEx(&c2, attn_combine_kernel<HD, float>, p);
+    }
+    if (e != cudaSuccess) {
+        set_error("attention (engine): %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    return FP4X_OK;
+}
+
+int launch_engine(cudaStream_t stream, const Params &p, uint32_t head_dim, bool pdl) {
+    const uint32_t hpc = heads_per_cta(p.n_heads / p.n_kv, true);
+    if (head_dim == 64 && hpc == 8) return launch_engine_t<64, 8>(stream, p, pdl);
+    if (head_dim == 64 && hpc == 4) return launch_engine_t<64, 4>(stream, p, pdl);
+    if (head_dim == 64 && hpc == 1) return launch_engine_t<64, 1>(stream, p, pdl);
+    if (head_dim == 128 && hpc == 8) return launch_engine_t<128, 8>(stream, p, pdl);
+    if (head_dim == 128 && hpc == 4) return launch_engine_t<128, 4>(stream, p, pdl);
+    if (head_dim == 128 && hpc == 1) return launch_engine_t<128, 1>(stream, p, pdl);
+    set_error("attention (engine): unsupported head_dim %u", head_dim);
+    return FP4X_EUNSUPPORTED;
 }
 
 }  // namespace attn

@@ -237,7 +237,7 @@ namespace fp4x {
 // Thread-local last-error message, returned by fp4x_last_error().
 void set_error(const char *fmt, ...);
 int check_launch(const char *what);
-inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int num_sms();
 }  // namespace fp4x
 

@@ -5,3 +5,4 @@
 #include "gemv.cu"
 #include "elementwise.cu"
 #include "attention.cu"
+#include "engine.cu"

@@ -13,6 +13,8 @@
 namespace fp4x {
 namespace quant {
 
+enum { ROWMAP_IDENTITY = 0, ROWMAP_ROPE_PAIRS = 1, ROWMAP_INTERLEAVE8 = 2 };
+
 __device__ __forceinline__ uint32_t nearest_code(float v) {
     // llama_run/src/main.rs:332,348-363
     const float levels[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
@@ -145,8 +147,55 @@ __global__ void init_mxfp4_kernel(uint64_t seed, float sigma, uint64_t nblocks, 
     scales[blk] = s;
 }
 
+// Destination row of source row r for the engine's fused layouts.
+//   ROWMAP_IDENTITY:  r + off
+//   ROWMAP_ROPE_PAIRS: rows of each head regrouped into 16-row tiles whose rows
+//     0..7 are head rows j0..j0+7 and rows 8..15 are j0+hd/2..j0+hd/2+7, so a
+//     rotate-half pair (j, j+hd/2) lands in one mma tile (rows g, g+8)
+//   ROWMAP_INTERLEAVE8: 8-row groups interleaved with a partner tensor in
+//     16-row tiles (gate rows at off 0, up rows at off 8)
+__device__ __forceinline__ uint32_t map_row(uint32_t r, int mode, uint32_t off, uint32_t hd) {
+    if (mode == ROWMAP_ROPE_PAIRS) {
+        const uint32_t half = hd / 2, head = r / hd, j = r % hd;
+        const uint32_t jj = j < half ? j : j - half;
+        return off + (head * (half / 8) + jj / 8) * 16 + (j < half ? 0u : 8u) + jj % 8;
+    }
+    if (mode == ROWMAP_INTERLEAVE8) return (r / 8) * 16 + (r % 8) + off;
+    return r + off;
+}
+
+__global__ void init_mxfp4_rowmap_kernel(uint64_t seed, float sigma, uint32_t n, uint32_t k, uint8_t *__restrict__ packed,
+                                         uint8_t *__restrict__ scales, int mode, uint32_t off, uint32_t hd) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t nbr = k / 32;
+    if (blk >= (uint64_t)n * nbr) return;
+    const uint32_t r = (uint32_t)(blk / nbr), b = (uint32_t)(blk % nbr);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = normal_draw(seed, blk * 32 + i, sigma);
+    uint4 p;
+    uint8_t s;
+    quant_block_mxfp4(v, p, s);
+    const uint64_t dblk = (uint64_t)map_row(r, mode, off, hd) * nbr + b;
+    reinterpret_cast<uint4 *>(packed)[dblk] = p;
+    scales[dblk] = s;
+}
+
 inline unsigned grid_for(uint64_t n, unsigned block) { return (unsigned)((n + block - 1) / block); }
 
+}  // namespace quant
+}  // namespace fp4x
+
+namespace fp4x {
+namespace quant {
+// Engine helper: generate tensor `seed` ([n][k], N(0, sigma)) straight into a
+// fused layout (row map above).
+int init_mxfp4_rowmap(cudaStream_t stream, uint64_t seed, float sigma, uint32_t n, uint32_t k, uint8_t *packed,
+                      uint8_t *scales, int mode, uint32_t off, uint32_t hd) {
+    const uint64_t nb = (uint64_t)n * (k / 32);
+    init_mxfp4_rowmap_kernel<<<grid_for(nb, 128), 128, 0, stream>>>(seed, sigma, n, k, packed, scales, mode, off, hd);
+    return check_launch("init_mxfp4_rowmap");
+}
 }  // namespace quant
 }  // namespace fp4x
 

@@ -93,3 +93,6 @@ def check(status: int) -> None:
 
 
 from . import ops  # noqa: E402,F401  (torch-facing wrappers)
+from . import engine  # noqa: E402,F401  (decode engine)
+
+EXTRA_SIGNATURES = engine.SIGNATURES

@@ -1,0 +1,137 @@
+"""Python mirror of the decode-engine part of the C ABI (llama_model_*,
+llama_forward, llama_decode_step, llama_generate).  Host buffers are numpy
+arrays; the model lives on the current CUDA device."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import check, lib
+
+TINYLLAMA = dict(n_layers=22, dim=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim=64, vocab=32000,
+                 max_seq=2048, rope_theta=10000.0, eps=1e-5, seed=0x5EED)
+LLAMA3_8B = dict(n_layers=32, dim=4096, ffn=14336, n_heads=32, n_kv_heads=8, head_dim=128, vocab=128256,
+                 max_seq=8192, rope_theta=500000.0, eps=1e-5, seed=0x5EED)
+
+
+class Config(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_uint32), ("dim", C.c_uint32), ("ffn", C.c_uint32),
+        ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
+        ("vocab", C.c_uint32), ("max_seq", C.c_uint32),
+        ("rope_theta", C.c_float), ("eps", C.c_float), ("seed", C.c_uint64),
+        ("tp_rank", C.c_uint32), ("tp_size", C.c_uint32),
+    ]
+
+
+_u8p = C.POINTER(C.c_uint8)
+_u16p = C.POINTER(C.c_uint16)
+_u32p = C.POINTER(C.c_uint32)
+_f32p = C.POINTER(C.c_float)
+
+SIGNATURES = {
+    "llama_model_create": (C.c_int, [C.POINTER(Config), C.POINTER(C.c_void_p)]),
+    "llama_model_destroy": (C.c_int, [C.c_void_p]),
+    "llama_model_reset": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "llama_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, _u32p, _f32p]),
+    "llama_decode_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "llama_generate": (C.c_int, [C.c_void_p, C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
+    "llama_model_export_tensor": (C.c_int, [C.c_void_p, C.c_uint32, _u8p, _u8p, _u32p, _u32p]),
+    "llama_model_embedding": (C.c_int, [C.c_void_p, _u16p]),
+    "llama_model_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "llama_model_kernels_per_token": (C.c_uint32, [C.c_void_p]),
+}
+
+
+def _declare():
+    L = lib()
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
+
+
+def _p(a, ct):
+    return a.ctypes.data_as(C.POINTER(ct))
+
+
+class Model:
+    """A random-init Llama-shape MXFP4 model on the current CUDA device."""
+
+    def __init__(self, cfg: dict, stream: int | None = None):
+        self.L = _declare()
+        self.cfg = dict(cfg)
+        c = Config(**{k: self.cfg.get(k, 0) for k, _ in Config._fields_})
+        if c.tp_size == 0:
+            c.tp_size = 1
+        self._c = c
+        h = C.c_void_p()
+        check(self.L.llama_model_create(C.byref(c), C.byref(h)))
+        self._h = h
+        self.stream = stream
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.L.llama_model_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _st(self):
+        if self.stream is not None:
+            return self.stream
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+
+    def reset(self):
+        check(self.L.llama_model_reset(self._h, self._st()))
+
+    def forward(self, token: int, pos: int, want_logits: bool = True):
+        nxt = np.zeros(1, np.uint32)
+        logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        check(self.L.llama_forward(self._h, self._st(), token, pos, _p(nxt, C.c_uint32),
+                                   _p(logits, C.c_float) if want_logits else None))
+        return int(nxt[0]), logits
+
+    def decode_step(self):
+        check(self.L.llama_decode_step(self._h, self._st()))
+
+    def generate(self, prompt, n_gen: int):
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(n_gen, np.uint32)
+        pre, dec = C.c_float(0), C.c_float(0)
+        check(self.L.llama_generate(self._h, self._st(), _p(prompt, C.c_uint32), len(prompt), n_gen,
+                                    _p(out, C.c_uint32), C.byref(pre), C.byref(dec)))
+        return out, pre.value, dec.value
+
+    def export_tensor(self, tensor_id: int):
+        n, k = C.c_uint32(0), C.c_uint32(0)
+        check(self.L.llama_model_export_tensor(self._h, tensor_id, None, None, C.byref(n), C.byref(k)))
+        packed = np.empty((n.value, k.value // 2), np.uint8)
+        scales = np.empty((n.value, k.value // 32), np.uint8)
+        check(self.L.llama_model_export_tensor(self._h, tensor_id, _p(packed, C.c_uint8), _p(scales, C.c_uint8),
+                                               None, None))
+        return packed, scales
+
+    def embedding(self):
+        e = np.empty((self.cfg["vocab"], self.cfg["dim"]), np.uint16)
+        check(self.L.llama_model_embedding(self._h, _p(e, C.c_uint16)))
+        return e
+
+    def kernels_per_token(self) -> int:
+        return int(self.L.llama_model_kernels_per_token(self._h))
+
+    def weight_bytes(self) -> int:
+        return int(self.L.llama_model_weight_bytes(self._h))

@@ -1,0 +1,139 @@
+"""Decode engine vs the CPU oracle: weights bit-exact, logits within 1e-2, same
+greedy tokens (BASELINE config 1 and small shapes).  All calls go through the C
+ABI (llama_model_create / llama_forward / llama_generate)."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_rms
+
+torch = pytest.importorskip("torch")
+from fp4x import engine  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-2
+
+TINY = dict(n_layers=2, dim=256, ffn=512, n_heads=8, n_kv_heads=2, head_dim=64, vocab=1000, max_seq=64,
+            rope_theta=10000.0, eps=1e-5, seed=1234)
+TINY128 = dict(n_layers=2, dim=512, ffn=1024, n_heads=8, n_kv_heads=4, head_dim=128, vocab=777, max_seq=48,
+               rope_theta=500000.0, eps=1e-5, seed=99)
+
+
+def tensor_ids(cfg):
+    ids = [1]
+    for l in range(cfg["n_layers"]):
+        ids += [16 + 8 * l + m for m in range(7)]
+    return ids
+
+
+def shape_of(cfg, tid):
+    if tid == 1:
+        return cfg["vocab"], cfg["dim"]
+    m = (tid - 16) % 8
+    qd, kvd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    return {0: (qd, cfg["dim"]), 1: (kvd, cfg["dim"]), 2: (kvd, cfg["dim"]), 3: (cfg["dim"], qd),
+            4: (cfg["ffn"], cfg["dim"]), 5: (cfg["ffn"], cfg["dim"]), 6: (cfg["dim"], cfg["ffn"])}[m]
+
+
+def compare_logits(got, ref):
+    """1e-2 relative (rms floor) and the same greedy token unless the reference's
+    top-2 margin is inside the tolerance band."""
+    err = rel_rms(got, ref).max()
+    assert err <= LOGIT_TOL, err
+    a, b = int(np.argmax(got)), int(np.argmax(ref))
+    if a != b:
+        top2 = np.sort(ref)[-2:]
+        margin = (top2[1] - top2[0]) / np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+        assert margin < LOGIT_TOL, f"argmax {a} vs {b} with margin {margin:.3e}"
+    return err
+
+
+@pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
+def test_engine_weights_bit_exact(cfg):
+    ref = oracle.Model(cfg)
+    with engine.Model(cfg) as m:
+        for tid in tensor_ids(cfg):
+            n, k = shape_of(cfg, tid)
+            gp, gs = m.export_tensor(tid)
+            rp, rs = ref.tensor(tid, n, k)
+            np.testing.assert_array_equal(gs, rs, err_msg=f"scales of tensor {tid}")
+            np.testing.assert_array_equal(gp, rp, err_msg=f"nibbles of tensor {tid}")
+        np.testing.assert_array_equal(m.embedding(), ref.embed())
+    ref.close()
+
+
+@pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
+def test_engine_forward_vs_oracle(cfg):
+    ref = oracle.Model(cfg)
+    toks = oracle.uniform_ids(5, cfg["vocab"], 40)
+    with engine.Model(cfg) as m:
+        for pos, t in enumerate(toks):
+            gn, gl = m.forward(int(t), pos)
+            rn, rl = ref.forward(int(t), pos)
+            compare_logits(gl, rl)
+            assert gn == int(np.argmax(gl))
+    ref.close()
+
+
+def test_engine_generate_equals_forward_loop():
+    prompt = oracle.uniform_ids(8, TINY["vocab"], 5)
+    with engine.Model(TINY) as m:
+        ids, pre_ms, dec_ms = m.generate(prompt, 20)
+        assert pre_ms > 0 and dec_ms > 0
+        m.reset()
+        seq = list(prompt)
+        loop = []
+        for pos in range(len(prompt) + 19):
+            nxt, _ = m.forward(int(seq[pos]), pos, want_logits=False)
+            if pos + 1 >= len(prompt):
+                loop.append(nxt)
+                seq.append(nxt)
+        np.testing.assert_array_equal(ids, np.array(loop, np.uint32))
+        # decode_step continues from the device-resident state left by generate
+        m.decode_step()
+        torch.cuda.synchronize()
+
+
+def test_engine_generate_matches_oracle_tiny():
+    prompt = oracle.uniform_ids(3, TINY["vocab"], 6)
+    ref = oracle.Model(TINY)
+    want = ref.generate(prompt, 24)
+    with engine.Model(TINY) as m:
+        got, _, _ = m.generate(prompt, 24)
+    ref.close()
+    np.testing.assert_array_equal(got, want)
+
+
+def test_engine_rejects_bad_config():
+    bad = dict(TINY, head_dim=96)
+    with pytest.raises(Exception):
+        engine.Model(bad)
+
+
+def test_engine_tinyllama_config1():
+    """22 layers, d 2048, ffn 5632, 32q/4kv, hd 64, V 32000, theta 1e4;
+    16 seeded prompt ids, 128 greedy tokens.  Weights bit-exact (sampled tensors),
+    logits within 1e-2 at every position, the same greedy tokens (teacher forcing
+    through the GPU's own sequence)."""
+    cfg = dict(engine.TINYLLAMA, max_seq=256)
+    prompt = oracle.uniform_ids(oracle.hash64(cfg["seed"], 2), cfg["vocab"], 16)
+    ref = oracle.Model(cfg)
+    with engine.Model(cfg) as m:
+        for tid in (1, 16, 16 + 2, 16 + 8 * 21 + 6):
+            n, k = shape_of(cfg, tid)
+            gp, gs = m.export_tensor(tid)
+            rp, rs = ref.tensor(tid, n, k)
+            np.testing.assert_array_equal(gs, rs)
+            np.testing.assert_array_equal(gp, rp)
+        ids, _, _ = m.generate(prompt, 128)
+        m.reset()
+        seq = list(prompt) + list(ids)
+        worst = 0.0
+        for pos in range(len(prompt) + 127):
+            gn, gl = m.forward(int(seq[pos]), pos)
+            rn, rl = ref.forward(int(seq[pos]), pos)
+            worst = max(worst, compare_logits(gl, rl))
+            if pos + 1 >= len(prompt):
+                assert gn == seq[pos + 1]
+    ref.close()
+    print(f"config1: worst logits rel err {worst:.3e}")
