@@ -149,6 +149,21 @@ FP4X_API int llama_attn_decode_bf16(fp4x_stream_t stream, uint32_t batch, uint32
                            uint32_t head_dim, uint32_t seq, uint32_t max_seq, const uint16_t *q,
                            const uint16_t *kc, const uint16_t *vc, uint16_t *out, void *workspace,
                            size_t workspace_bytes);
+/* No counterpart in the reference: an allocation-free llama_attn_decode_bf16
+ * for callers that cannot allocate device memory (their device memory belongs
+ * to a pool allocator of the host, or their serving loop forbids cudaMalloc /
+ * cudaFree).  The split-KV partials live in one static device array of
+ * llama_attn_noalloc_max_bytes() bytes (4 MiB) that every GPU loading the
+ * library keeps until exit; a shape needing more returns FP4X_EINVAL.  The
+ * first call on each device looks the array up (make it before any stream
+ * capture).  Calls share the array: calls that overlap on the GPU race, so
+ * issue them on one stream. */
+FP4X_API int llama_attn_decode_bf16_noalloc(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads,
+                                            uint32_t n_kv_heads, uint32_t head_dim, uint32_t seq, uint32_t max_seq,
+                                            const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
+                                            uint16_t *out);
+/* Size of the static scratch array used by llama_attn_decode_bf16_noalloc. */
+FP4X_API size_t llama_attn_noalloc_max_bytes(void);
 /* The decode engine's form: f32 q and out, bf16 caches. */
 FP4X_API int llama_attn_decode_f32q_bf16kv(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
                                   uint32_t head_dim, uint32_t seq, uint32_t max_seq, const float *q,

@@ -19,6 +19,7 @@
 #include "attention.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace fp4x {
 namespace attn {
@@ -353,4 +354,81 @@ extern "C" int llama_attn_decode_f32q_bf16kv(fp4x_stream_t stream, uint32_t batc
                                              void *workspace, size_t workspace_bytes) {
     return attn::run<float, uint16_t, float>((cudaStream_t)stream, batch, n_heads, n_kv_heads, head_dim, seq, max_seq,
                                              q, kc, vc, out, workspace, workspace_bytes, true);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of llama_attn_decode_bf16.
+//
+// Some callers cannot allocate device memory for the split-KV partials: a host
+// whose device memory is owned by its own pool allocator and must not see a
+// cudaMalloc from inside a plugin, or a latency-critical serving loop where
+// cudaMalloc/cudaFree (which can synchronise the device) are not allowed.  For
+// them the partials live in one file-scope __device__ array of fixed size,
+// kNoAllocScratchFloats floats (4 MiB), which every GPU that loads this library
+// holds until the process exits.  In host code the array's name is only a
+// host-side stand-in, so its device address is looked up once per device with
+// cudaGetSymbolAddress (on the first call made with that device current; make
+// that first call before any stream capture) and cached.
+//
+// All calls share the array and it keeps the last call's contents.  Nothing in
+// it has to start at zero: every slice record a call reads was written earlier
+// in the same call.  Calls whose kernels overlap on the GPU (different streams,
+// or host threads racing on one device) write the same memory and race; callers
+// must serialise them, e.g. by issuing them on one stream.
+namespace fp4x {
+namespace attn {
+
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+static float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(float **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error("llama_attn_decode_bf16_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    FP4X_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "llama_attn_decode_bf16_noalloc: device %d out of range",
+                 dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("llama_attn_decode_bf16_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+            return FP4X_ECUDA;
+        }
+        g_noalloc_ptr[dev] = static_cast<float *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return FP4X_OK;
+}
+
+}  // namespace attn
+}  // namespace fp4x
+
+extern "C" size_t llama_attn_noalloc_max_bytes(void) { return attn::kNoAllocScratchFloats * sizeof(float); }
+
+extern "C" int llama_attn_decode_bf16_noalloc(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads,
+                                              uint32_t n_kv_heads, uint32_t head_dim, uint32_t seq, uint32_t max_seq,
+                                              const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
+                                              uint16_t *out) {
+    FP4X_REQUIRE(n_kv_heads > 0 && n_heads % n_kv_heads == 0, "llama_attn_decode_bf16_noalloc: n_heads %% n_kv != 0");
+    const size_t need = llama_attn_workspace_size(batch, n_heads, n_kv_heads, head_dim, seq);
+    const size_t cap = attn::kNoAllocScratchFloats * sizeof(float);
+    FP4X_REQUIRE(need <= cap,
+                 "llama_attn_decode_bf16_noalloc: this shape needs %zu bytes of split-KV scratch, above the %zu-byte "
+                 "static maximum; use llama_attn_decode_bf16 with a caller workspace",
+                 need, cap);
+    float *scratch = nullptr;
+    if (need > 0) {
+        const int st = attn::noalloc_scratch(&scratch);
+        if (st) return st;
+    }
+    return attn::run<uint16_t, uint16_t, uint16_t>((cudaStream_t)stream, batch, n_heads, n_kv_heads, head_dim, seq,
+                                                   max_seq, q, kc, vc, out, scratch, need ? cap : 0, true);
 }

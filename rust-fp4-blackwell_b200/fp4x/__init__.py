@@ -66,6 +66,8 @@ SIGNATURES = {
                                          _vp, _vp, _vp, _vp, _vp, _sz]),
     "llama_attn_decode_f32q_bf16kv": (C.c_int, [_vp, _u32, _u32, _u32, _u32, _u32, _u32,
                                                 _vp, _vp, _vp, _vp, _vp, _sz]),
+    "llama_attn_decode_bf16_noalloc": (C.c_int, [_vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp]),
+    "llama_attn_noalloc_max_bytes": (_sz, []),
 }
 
 
