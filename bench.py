@@ -257,8 +257,7 @@ def main():
 
     # prefill the prompt (device-resident loop); the last prompt position yields token 1
     model.generate(prompt, 1)
-    for _ in range(args.warmup):
-        model.decode_step()
+    model.decode_steps(args.warmup)
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -267,8 +266,7 @@ def main():
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         e0.record(st)
-        for _ in range(args.steps):
-            model.decode_step()
+        model.decode_steps(args.steps)  # K tokens of the device-resident loop
         e1.record(st)
         torch.cuda.synchronize()
     if dist:
@@ -281,8 +279,9 @@ def main():
     value = world * args.steps / t
     per_tok = t / args.steps
     wbytes = model.weight_bytes()
+    model_path = model.path
     achieved = wbytes / per_tok / 1e9
-    kpt = model.kernels_per_token()
+    kpt = model.kernels_per_token() if model.path == "graph" else 1
 
     e2e = None
     if not args.no_e2e:
@@ -327,13 +326,13 @@ def main():
                    "positions": f"{N_PROMPT}..{N_PROMPT + args.warmup + args.steps - 1}",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "no flush: 549.5 MB of weights per step > 126 MB L2"},
-        "roofline": {"bound": "hbm", "kernel": "decode token (CUDA graph of fused GEMV + attention kernels)",
+        "roofline": {"bound": "hbm", "kernel": f"decode token ({model_path} path)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "bytes_per_launch": wbytes, "peak_kind": peak_kind},
         "gemv": gemv,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": kpt * args.steps,
+        "gpu_launches": kpt * args.steps if model_path == "graph" else 1,
         "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"]},
     }
     if rank == 0:

@@ -203,6 +203,14 @@ FP4X_API int llama_forward(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t t
 /* One token of the device-resident loop (decode_step, llama_decode/src/main.rs:428-477):
  * consumes the device token/position left by the previous step, asynchronous. */
 FP4X_API int llama_decode_step(fp4x_llama_model *m, fp4x_stream_t stream);
+/* n tokens of the device-resident loop in one call (one launch on the
+ * persistent path). */
+FP4X_API int llama_decode_steps(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t n);
+/* Decode path: 1 = persistent kernel (one cooperative launch runs many tokens;
+ * default when the shape fits), 0 = CUDA graph of fused per-layer kernels.
+ * The environment variable FP4X_DECODE_PATH=graph selects 0 at creation. */
+FP4X_API int llama_model_set_path(fp4x_llama_model *m, int path);
+FP4X_API int llama_model_get_path(const fp4x_llama_model *m);
 /* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-587, EOS
  * ignored): prefill the prompt one position at a time, then n_gen tokens.
  * prompt/out_ids are HOST arrays; *prefill_ms covers the n_prompt forwards (the

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
     constexpr uint32_t H = HPC;
     const uint32_t h0 = hgrp * H;
     const uint32_t group = p.n_heads / p.n_kv, kvh = h0 / group;
-    const uint32_t seq = p.pos_ptr ? *p.pos_ptr + 1 : p.seq;
+    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
     const uint32_t t_begin = split * p.split_len, t_end = min(seq, t_begin + p.split_len);
     if (t_begin >= seq) return;  // slice past the current position (whole CTA, before any barrier)
 
@@ -200,7 +200,7 @@ __global__ void attn_combine_kernel(Params p) {
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const size_t bh = (size_t)b * p.n_heads + h;
     const float *rec = p.ws + bh * p.splits * (HD + 2);
-    const uint32_t seq = p.pos_ptr ? *p.pos_ptr + 1 : p.seq;
+    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
     const uint32_t used = (seq + p.split_len - 1) / p.split_len;
     float M = -INFINITY;
     for (uint32_t s = 0; s < used; ++s) M = fmaxf(M, rec[s * (HD + 2)]);

@@ -31,10 +31,11 @@ __device__ uint32_t g_device_error = 0;
 
 __device__ __forceinline__ void raise_device_error(uint32_t bit) { atomicOr(&g_device_error, bit); }
 
-// Upper bound on polling iterations of any spin-wait (each poll backs off with
-// a suspend hint / nanosleep, so this is seconds of wall time, far above any
-// legitimate wait and far below a watchdog).
-constexpr uint32_t kSpinLimit = 1u << 24;
+// Upper bound on polling iterations of any mbarrier spin-wait.  Each poll may
+// suspend for at most kSuspendHintNs, so the bound is ~2 s of wall time: far
+// above any legitimate wait, far below a watchdog.
+constexpr uint32_t kSpinLimit = 1u << 21;
+constexpr uint32_t kSuspendHintNs = 1000;
 
 // ---------------------------------------------------------------- smem/mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -70,7 +71,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
         "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(phase), "r"(1000000u)
+        : "r"(smem_u32(bar)), "r"(phase), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }

@@ -22,6 +22,8 @@
 #include "common.cuh"
 #include "gemv.cuh"
 
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -68,6 +70,13 @@ struct fp4x_llama_model {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool pdl = true;
+    // contiguous [n_layers][...] blocks shared by both decode paths
+    float *norms = nullptr;        // attn norms [L][dim] then ffn norms [L][dim]
+    uint16_t *kv = nullptr;        // K [L][max_seq][kvd] then V [L][max_seq][kvd]
+    fp4x::persist::Engine *pe = nullptr;  // persistent decode kernel (null: unsupported shape)
+    int path = 0;                  // 0: CUDA graph of fused kernels, 1: persistent kernel
+    int64_t hpos = -1;             // host view of the device-resident position (-1: unknown)
+    char persist_why[256] = "";    // why the persistent kernel is unavailable, if it is
 };
 
 namespace fp4x {
@@ -190,6 +199,7 @@ int enqueue_token(fp4x_llama_model *m, cudaStream_t st) {
         a.embed = m->embed, a.tok = tok, a.x_out = m->x;
         a.q_tiles = qd / 16, a.k_tiles = kvd / 16, a.n_kv = c.n_kv_heads, a.head_dim = hd;
         a.cos_t = m->cos_t, a.sin_t = m->sin_t, a.pos = pos, a.q_out = m->q, a.kc = L.kc, a.vc = L.vc;
+        a.max_seq = c.max_seq;
         FP4X_TRY(gemv::launch_fused(st, l == 0 ? gemv::PRO_EMBED_RMSNORM : gemv::PRO_RMSNORM, gemv::EPI_QKV_ROPE,
                                     a, pdl));
         // 2. attention over positions 0..pos
@@ -293,16 +303,18 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
         return r;
     };
     m->layers.resize(c.n_layers);
+    rc = alloc(m, &m->norms, (size_t)2 * c.n_layers * c.dim);
+    if (!rc) rc = alloc(m, &m->kv, (size_t)2 * c.n_layers * c.max_seq * kvd);
     for (uint32_t l = 0; l < c.n_layers && !rc; ++l) {
         LayerW &L = m->layers[l];
         rc = alloc_q(m, L.qkv, qd + 2 * kvd, c.dim);
         if (!rc) rc = alloc_q(m, L.o, c.dim, qd);
         if (!rc) rc = alloc_q(m, L.gu, 2 * c.ffn, c.dim);
         if (!rc) rc = alloc_q(m, L.down, c.dim, c.ffn);
-        if (!rc) rc = alloc(m, &L.attn_norm, c.dim);
-        if (!rc) rc = alloc(m, &L.ffn_norm, c.dim);
-        if (!rc) rc = alloc(m, &L.kc, (size_t)c.max_seq * kvd);
-        if (!rc) rc = alloc(m, &L.vc, (size_t)c.max_seq * kvd);
+        L.attn_norm = m->norms + (size_t)l * c.dim;
+        L.ffn_norm = m->norms + (size_t)(c.n_layers + l) * c.dim;
+        L.kc = m->kv + (size_t)l * c.max_seq * kvd;
+        L.vc = m->kv + (size_t)(c.n_layers + l) * c.max_seq * kvd;
     }
     if (!rc) rc = alloc_q(m, m->lm_head, c.vocab, c.dim);
     if (!rc) rc = alloc(m, &m->embed, (size_t)c.vocab * c.dim);
@@ -331,8 +343,48 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
             rc = cuda_fail("llama_model_create: init", cudaGetLastError());
     }
     if (!rc) rc = build_graph(m);
+    if (!rc) {
+        persist::BuildIn in;
+        in.cfg = c;
+        for (auto &L : m->layers) {
+            in.qkv.push_back({L.qkv.w, L.qkv.s, L.qkv.n, L.qkv.k});
+            in.o.push_back({L.o.w, L.o.s, L.o.n, L.o.k});
+            in.gu.push_back({L.gu.w, L.gu.s, L.gu.n, L.gu.k});
+            in.down.push_back({L.down.w, L.down.s, L.down.n, L.down.k});
+        }
+        in.lm = {m->lm_head.w, m->lm_head.s, m->lm_head.n, m->lm_head.k};
+        in.attn_norm = m->norms, in.ffn_norm = m->norms + (size_t)c.n_layers * c.dim, in.final_norm = m->final_norm;
+        in.embed = m->embed, in.cos_t = m->cos_t, in.sin_t = m->sin_t;
+        in.kc = m->kv, in.vc = m->kv + (size_t)c.n_layers * c.max_seq * kvd;
+        in.q = m->q, in.logits = m->logits, in.state = m->state, in.prompt = m->prompt, in.out = m->out;
+        const int prc = persist::build(in, m->cap_stream, &m->pe);
+        if (prc == FP4X_OK) {
+            m->path = 1;
+        } else if (prc == FP4X_EUNSUPPORTED) {
+            m->pe = nullptr;  // graph path only
+            snprintf(m->persist_why, sizeof(m->persist_why), "%s", fp4x_last_error());
+        } else {
+            rc = prc;
+        }
+        const char *env = getenv("FP4X_DECODE_PATH");
+        if (env && strcmp(env, "graph") == 0) m->path = 0;
+    }
     if (rc) return fail(rc);
     *out = m;
+    return FP4X_OK;
+}
+
+// Run n tokens of the device-resident loop on the selected path.
+int run_tokens(fp4x_llama_model *m, cudaStream_t st, uint32_t n) {
+    FP4X_REQUIRE(m->hpos >= 0, "decode: no position set (call llama_forward or llama_generate first)");
+    FP4X_REQUIRE((uint64_t)m->hpos + n <= m->cfg.max_seq, "decode: position %lld + %u tokens exceeds max_seq %u",
+                 (long long)m->hpos, n, m->cfg.max_seq);
+    if (m->path == 1) {
+        FP4X_TRY(persist::launch(m->pe, st, n));
+    } else {
+        for (uint32_t i = 0; i < n; ++i) FP4X_CUDA(cudaGraphLaunch(m->exec, st));
+    }
+    m->hpos += n;
     return FP4X_OK;
 }
 
@@ -340,6 +392,7 @@ int set_state(fp4x_llama_model *m, cudaStream_t st, uint32_t tok, uint32_t pos, 
     // pageable source: the copy is staged before the call returns
     const uint32_t v[5] = {tok, pos, 0, n_prompt, cap};
     FP4X_CUDA(cudaMemcpyAsync(m->state, v, sizeof(v), cudaMemcpyHostToDevice, st));
+    m->hpos = pos;
     return FP4X_OK;
 }
 
@@ -362,6 +415,7 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
         cudaStreamSynchronize(m->cap_stream);
         cudaStreamDestroy(m->cap_stream);
     }
+    persist::destroy(m->pe);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return FP4X_OK;
@@ -370,18 +424,32 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
 extern "C" int llama_model_reset(fp4x_llama_model *m, fp4x_stream_t stream) {
     FP4X_REQUIRE(m, "llama_model_reset: null model");
     const uint32_t kvd = m->cfg.n_kv_heads * m->cfg.head_dim;
-    for (auto &L : m->layers) {
-        FP4X_CUDA(cudaMemsetAsync(L.kc, 0, (size_t)m->cfg.max_seq * kvd * 2, (cudaStream_t)stream));
-        FP4X_CUDA(cudaMemsetAsync(L.vc, 0, (size_t)m->cfg.max_seq * kvd * 2, (cudaStream_t)stream));
-    }
+    FP4X_CUDA(cudaMemsetAsync(m->kv, 0, (size_t)2 * m->cfg.n_layers * m->cfg.max_seq * kvd * 2,
+                              (cudaStream_t)stream));
     return FP4X_OK;
 }
 
 extern "C" int llama_decode_step(fp4x_llama_model *m, fp4x_stream_t stream) {
     FP4X_REQUIRE(m && m->exec, "llama_decode_step: null model");
-    FP4X_CUDA(cudaGraphLaunch(m->exec, (cudaStream_t)stream));
+    return run_tokens(m, (cudaStream_t)stream, 1);
+}
+
+extern "C" int llama_decode_steps(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t n) {
+    FP4X_REQUIRE(m && m->exec, "llama_decode_steps: null model");
+    return run_tokens(m, (cudaStream_t)stream, n);
+}
+
+extern "C" int llama_model_set_path(fp4x_llama_model *m, int path) {
+    FP4X_REQUIRE(m && (path == 0 || path == 1), "llama_model_set_path: bad argument");
+    if (path == 1 && !m->pe) {
+        set_error("llama_model_set_path: the persistent kernel is unavailable: %s", m->persist_why);
+        return FP4X_EUNSUPPORTED;
+    }
+    m->path = path;
     return FP4X_OK;
 }
+
+extern "C" int llama_model_get_path(const fp4x_llama_model *m) { return m ? m->path : -1; }
 
 extern "C" int llama_forward(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t token, uint32_t pos,
                              uint32_t *next_host, float *logits_host) {
@@ -390,7 +458,7 @@ extern "C" int llama_forward(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t
     FP4X_REQUIRE(pos < m->cfg.max_seq, "llama_forward: pos %u >= max_seq %u", pos, m->cfg.max_seq);
     cudaStream_t st = (cudaStream_t)stream;
     FP4X_TRY(set_state(m, st, token, pos, 0, 0));
-    FP4X_CUDA(cudaGraphLaunch(m->exec, st));
+    FP4X_TRY(run_tokens(m, st, 1));
     if (next_host) FP4X_CUDA(cudaMemcpyAsync(next_host, m->state + 2, 4, cudaMemcpyDeviceToHost, st));
     if (logits_host)
         FP4X_CUDA(cudaMemcpyAsync(logits_host, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
@@ -416,9 +484,9 @@ extern "C" int llama_generate(fp4x_llama_model *m, fp4x_stream_t stream, const u
     FP4X_CUDA(cudaEventRecord(e0, st));
     // prefill = the same one-token path over the prompt (llama_run:550-556); the
     // last prompt position yields the first generated token
-    for (uint32_t i = 0; i < n_prompt; ++i) FP4X_CUDA(cudaGraphLaunch(m->exec, st));
+    FP4X_TRY(run_tokens(m, st, n_prompt));
     FP4X_CUDA(cudaEventRecord(e1, st));
-    for (uint32_t i = 1; i < n_gen; ++i) FP4X_CUDA(cudaGraphLaunch(m->exec, st));
+    FP4X_TRY(run_tokens(m, st, n_gen - 1));
     FP4X_CUDA(cudaEventRecord(e2, st));
     FP4X_CUDA(cudaMemcpyAsync(out_ids, m->out, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, st));
     FP4X_CUDA(cudaStreamSynchronize(st));

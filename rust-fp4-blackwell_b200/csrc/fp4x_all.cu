@@ -5,4 +5,5 @@
 #include "gemv.cu"
 #include "elementwise.cu"
 #include "attention.cu"
+#include "persist.cu"
 #include "engine.cu"

@@ -317,6 +317,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Args a) {
         }
     } else if (EPI == EPI_QKV_ROPE) {
         const uint32_t pos = *a.pos;
+        if (pos >= a.max_seq) return;  // never write past the cache (host also bounds positions)
         const uint32_t hd = a.head_dim, half = hd / 2, tiles_per_head = half / 8;
         const uint32_t tile = blockIdx.x;
         const uint32_t kvrow = a.n_kv * hd;  // elements per position of one layer's cache

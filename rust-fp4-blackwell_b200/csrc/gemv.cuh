@@ -35,6 +35,7 @@ struct Args {
     uint32_t q_tiles, k_tiles, n_kv, head_dim;
     const float *cos_t, *sin_t;  // [max_seq][hd/2]
     const uint32_t *pos;         // device position
+    uint32_t max_seq;            // cache capacity (positions)
     float *q_out;                // [n_heads][hd]
     uint16_t *kc, *vc;           // this layer's cache [max_seq][n_kv][hd] bf16
 };

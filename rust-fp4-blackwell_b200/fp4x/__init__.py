@@ -72,10 +72,13 @@ SIGNATURES = {
 
 
 def lib():
-    """Load (building first if stale) libfp4x.so and declare every C-ABI symbol."""
+    """Load (building first if stale) libfp4x.so and declare every C-ABI symbol.
+    FP4X_LIB=<path> loads another build of the same library instead (e.g. one
+    compiled with extra instrumentation)."""
     global _lib
     if _lib is None:
-        path = _build.build()
+        import os
+        path = os.environ.get("FP4X_LIB") or _build.build()
         L = C.CDLL(str(path))
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(L, name)

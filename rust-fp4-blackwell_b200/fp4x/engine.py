@@ -41,6 +41,9 @@ SIGNATURES = {
     "llama_model_embedding": (C.c_int, [C.c_void_p, _u16p]),
     "llama_model_weight_bytes": (C.c_size_t, [C.c_void_p]),
     "llama_model_kernels_per_token": (C.c_uint32, [C.c_void_p]),
+    "llama_decode_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "llama_model_set_path": (C.c_int, [C.c_void_p, C.c_int]),
+    "llama_model_get_path": (C.c_int, [C.c_void_p]),
 }
 
 
@@ -107,6 +110,16 @@ class Model:
 
     def decode_step(self):
         check(self.L.llama_decode_step(self._h, self._st()))
+
+    def decode_steps(self, n: int):
+        check(self.L.llama_decode_steps(self._h, self._st(), n))
+
+    @property
+    def path(self) -> str:
+        return {0: "graph", 1: "persistent"}[self.L.llama_model_get_path(self._h)]
+
+    def set_path(self, path: str):
+        check(self.L.llama_model_set_path(self._h, {"graph": 0, "persistent": 1}[path]))
 
     def generate(self, prompt, n_gen: int):
         prompt = np.ascontiguousarray(prompt, np.uint32)

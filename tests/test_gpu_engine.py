@@ -62,11 +62,13 @@ def test_engine_weights_bit_exact(cfg):
     ref.close()
 
 
+@pytest.mark.parametrize("path", ["graph", "persistent"])
 @pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
-def test_engine_forward_vs_oracle(cfg):
+def test_engine_forward_vs_oracle(cfg, path):
     ref = oracle.Model(cfg)
     toks = oracle.uniform_ids(5, cfg["vocab"], 40)
     with engine.Model(cfg) as m:
+        m.set_path(path)
         for pos, t in enumerate(toks):
             gn, gl = m.forward(int(t), pos)
             rn, rl = ref.forward(int(t), pos)
@@ -75,9 +77,11 @@ def test_engine_forward_vs_oracle(cfg):
     ref.close()
 
 
-def test_engine_generate_equals_forward_loop():
+@pytest.mark.parametrize("path", ["graph", "persistent"])
+def test_engine_generate_equals_forward_loop(path):
     prompt = oracle.uniform_ids(8, TINY["vocab"], 5)
     with engine.Model(TINY) as m:
+        m.set_path(path)
         ids, pre_ms, dec_ms = m.generate(prompt, 20)
         assert pre_ms > 0 and dec_ms > 0
         m.reset()
@@ -94,14 +98,30 @@ def test_engine_generate_equals_forward_loop():
         torch.cuda.synchronize()
 
 
-def test_engine_generate_matches_oracle_tiny():
+@pytest.mark.parametrize("path", ["graph", "persistent"])
+def test_engine_generate_matches_oracle_tiny(path):
     prompt = oracle.uniform_ids(3, TINY["vocab"], 6)
     ref = oracle.Model(TINY)
     want = ref.generate(prompt, 24)
     with engine.Model(TINY) as m:
+        m.set_path(path)
         got, _, _ = m.generate(prompt, 24)
     ref.close()
     np.testing.assert_array_equal(got, want)
+
+
+def test_engine_default_path_is_persistent():
+    with engine.Model(TINY) as m:
+        assert m.path == "persistent"
+
+
+def test_engine_decode_steps_bounded_by_max_seq():
+    with engine.Model(TINY) as m:
+        m.generate(oracle.uniform_ids(1, TINY["vocab"], 4), 1)  # device position 4
+        with pytest.raises(Exception):
+            m.decode_steps(TINY["max_seq"])  # would run past the cache
+        m.decode_steps(TINY["max_seq"] - 4)  # exactly fills it
+        torch.cuda.synchronize()
 
 
 def test_engine_rejects_bad_config():
@@ -119,6 +139,7 @@ def test_engine_tinyllama_config1():
     prompt = oracle.uniform_ids(oracle.hash64(cfg["seed"], 2), cfg["vocab"], 16)
     ref = oracle.Model(cfg)
     with engine.Model(cfg) as m:
+        assert m.path == "persistent"
         for tid in (1, 16, 16 + 2, 16 + 8 * 21 + 6):
             n, k = shape_of(cfg, tid)
             gp, gs = m.export_tensor(tid)
