@@ -30,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -66,57 +65,70 @@ def hbm_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event reasons of this process's GPU, polled through NVML
+    every 5 ms while the timed region runs (read-only queries; nvidia-smi's 200 ms
+    floor would miss a sub-second region).  The device is found by PCI bus id."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.sm, self.bits, self.max_mhz = [], 0, None
+        self.err = None
+        self._stop = threading.Event()
+        self.t = None
+
+    def _handle(self, nv):
+        import torch
+        pr = torch.cuda.get_device_properties(self.cuda_index)
+        for fmt in ("{:08x}:{:02x}:{:02x}.0", "{:04x}:{:02x}:{:02x}.0"):
+            try:
+                return nv.nvmlDeviceGetHandleByPciBusId(fmt.format(pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id))
+            except Exception:
+                pass
+        return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv, self.h = nv, self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:  # no NVML: report no samples rather than fail the bench
+            self.err = repr(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self._stop.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                self.bits |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+            except Exception as e:
+                self.err = repr(e)
+                return
+            time.sleep(self.period)
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self.t:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = []
+        if self.t:
+            reasons = [name for name, attr in self.REASONS if self.bits & int(getattr(self.nv, attr, 0))]
+        out = {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+               "reasons": reasons, "samples": len(self.sm), "source": "nvml"}
+        if self.err:
+            out["error"] = self.err
+        return out
 
 
 def cpu_baseline_port(cfg, budget_s=20.0, threads=0):

@@ -99,6 +99,27 @@ FP4X_API int fp4_gemv_ref(fp4x_stream_t stream, uint32_t n, uint32_t k, const ui
 FP4X_API int fp4_gemv_f32x(fp4x_stream_t stream, uint32_t n, uint32_t k, const uint8_t *w, const uint8_t *scales,
                   const float *x, float *y);
 
+/* Block-scaled MXFP4 x MXFP4 GEMM on tcgen05.mma.kind::mxf4 (fp32 accumulate):
+ *   d[t][r] = sum_k A[t][k] * W[r][k],  A = a [m][k/2] nibbles + a_scales [m][k/32],
+ *   W = w [n][k/2] + w_scales [n][k/32] (E8M0), d = [m][n].
+ * The reference's MMA is the single-warp m16n8k64 known-answer test
+ * fp4_mma_allones (examples/fp4_mma/src/main.rs:18-54, sm_120a mma.sync); this
+ * is the batched-decode / prefill GEMM built on it.  k must be a multiple of 64;
+ * a and w 16-byte aligned.  When the tile grid is too small to fill the GPU the
+ * K range is split and partial sums meet in an fp32 workspace of
+ * fp4_mma_workspace_size(m, n, k) bytes (0 = none needed; may then be NULL). */
+FP4X_API size_t fp4_mma_workspace_size(uint32_t m, uint32_t n, uint32_t k);
+FP4X_API int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                     const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, uint16_t *d_bf16,
+                     void *workspace, size_t workspace_bytes);
+/* Same GEMM with fp32 output (exact accumulator values; no workspace). */
+FP4X_API int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                         const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float *d);
+/* The reference's known-answer test on the tcgen05 path: A = B = all 1.0
+ * (bytes 0x22), every scale 2^0 (0x7F), K = 64; out[16*8] = D, every value 64.0.
+ * Replaces fp4_mma_allones, examples/fp4_mma/src/main.rs:18-54 (check :75-85). */
+FP4X_API int fp4_mma_allones(fp4x_stream_t stream, float *out);
+
 /* y = x * rsqrt(mean(x^2) + eps) * weight.  Replaces rmsnorm,
  * llama_run/src/main.rs:79-116 (test llama_rmsnorm/src/main.rs:14-56). */
 FP4X_API int llama_rmsnorm(fp4x_stream_t stream, uint32_t dim, float eps, const float *x, const float *weight,

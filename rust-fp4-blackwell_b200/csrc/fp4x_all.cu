@@ -5,5 +5,6 @@
 #include "gemv.cu"
 #include "elementwise.cu"
 #include "attention.cu"
+#include "mma.cu"
 #include "persist.cu"
 #include "engine.cu"

@@ -1,0 +1,421 @@
+// mma.cu -- fp4_mma: block-scaled MXFP4 x MXFP4 GEMM on the sm_100a tensor cores.
+//
+//   D[t][r] = sum_k A[t][k] * W[r][k],  A: [m][k] tokens, W: [n][k] weight rows,
+//   both packed E2M1 (k/2 bytes a row, low nibble = lower k) with one E8M0 scale
+//   per 32 values ([rows][k/32] bytes); fp32 accumulation, bf16 or fp32 out.
+//
+// The reference has no GEMM on this path, only the single-warp all-ones
+// known-answer test (examples/fp4_mma/src/main.rs:18-54: every D = 64.0) and
+// the m16n8k64 operand/scale layout notes it pins (trackb/FP4_M16N8K64_LAYOUT.md).
+// The CPU oracle's orc_mma_mxf4 restates the arithmetic.
+//
+// One CTA computes a 128-weight-row x NT-token tile (NT = 8..256) over a range
+// of K stages (256 k each, split-K when the tile grid alone cannot fill the
+// SMs).  Weights are the MMA's A operand (M = 128), tokens its B operand (N = NT):
+//   warp 0     TMA producer: one 128-byte-swizzled box of each operand a stage;
+//   warp 1     allocates tensor memory; lane 0 issues tcgen05.cp (scales) and
+//              4 x tcgen05.mma.kind::mxf4 a stage, then tcgen05.commit;
+//   warps 2-5  gather the stage's E8M0 scales into shared scale atoms, then run
+//              the epilogue (tcgen05.ld -> bf16/fp32 stores or fp32 red.add).
+#include "common.cuh"
+#include "tc05.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace fp4x {
+namespace tc {
+
+bool make_map_sw128(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tc
+
+namespace mma {
+
+constexpr int kThreads = 192;
+constexpr uint32_t kStageK = 256;             // k per stage: one 128-byte swizzle row
+constexpr uint32_t kTileA = 128 * 128;        // weight tile bytes per stage
+constexpr uint32_t kMaxStages = 8;
+constexpr uint32_t kSmemLimit = 227 * 1024;
+constexpr uint32_t kBarBytes = 256;
+
+enum Mode : uint32_t { OUT_BF16 = 0, OUT_F32 = 1, OUT_RED_F32 = 2 };
+
+struct Geo {
+    uint32_t nt, stages, sfb_atoms, stage_bytes, b_off, sfa_off, sfb_off, tmem_cols, sfa_col0, sfb_col0, smem;
+};
+
+__host__ __device__ inline Geo geometry(uint32_t nt) {
+    Geo g;
+    g.nt = nt;
+    g.sfb_atoms = nt > 128 ? 2 : 1;
+    g.b_off = kTileA;
+    g.sfa_off = g.b_off + nt * 128;
+    g.sfb_off = g.sfa_off + 2 * 512;
+    g.stage_bytes = (g.sfb_off + g.sfb_atoms * 2 * 512 + 1023) / 1024 * 1024;
+    uint32_t s = (kSmemLimit - 1024 - kBarBytes) / g.stage_bytes;
+    g.stages = s > kMaxStages ? kMaxStages : s;
+    g.sfa_col0 = nt;
+    g.sfb_col0 = nt + g.stages * 8;
+    const uint32_t cols = g.sfb_col0 + g.stages * 8 * g.sfb_atoms;
+    uint32_t c = 32;
+    while (c < cols) c *= 2;
+    g.tmem_cols = c;
+    g.smem = g.stages * g.stage_bytes + 1024 + kBarBytes;
+    return g;
+}
+
+struct Args {
+    uint32_t m, n, k, nt, kps;  // kps: K stages per split
+    const uint8_t *sa, *sw;     // scales [m][k/32], [n][k/32]
+    void *d;                    // [m][n] bf16 or f32
+    uint32_t mode;
+};
+
+// Bounded wait that also gives up when another role of the CTA has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    *abort = 1;
+    raise_device_error(DEVERR_MBAR_TIMEOUT);
+    return false;
+}
+
+// 8 scale bytes [kb0, kb0 + 8) of one row (0 outside the matrix).
+__device__ __forceinline__ uint2 load_scales8(const uint8_t *s, uint32_t row, uint32_t rows, uint32_t kb0,
+                                              uint32_t kbt) {
+    if (row >= rows) return make_uint2(0, 0);
+    const uint8_t *p = s + (size_t)row * kbt + kb0;
+    if ((kbt & 7u) == 0 && kb0 + 8 <= kbt) return __ldg(reinterpret_cast<const uint2 *>(p));
+    uint32_t w[2] = {0, 0};
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j)
+        if (kb0 + j < kbt) w[j >> 2] |= (uint32_t)__ldg(p + j) << (8 * (j & 3));
+    return make_uint2(w[0], w[1]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mxf4_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a, Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const Geo G = geometry(a.nt);
+    const uint32_t S = G.stages;
+    uint64_t *full_t = reinterpret_cast<uint64_t *>(smem + S * G.stage_bytes);  // TMA bytes landed
+    uint64_t *full_s = full_t + kMaxStages;                                     // scale atoms written
+    uint64_t *empty = full_s + kMaxStages;                                      // MMAs of the stage done
+    uint64_t *accb = empty + kMaxStages;                                        // accumulator complete
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accb + 1);
+    volatile uint32_t *abort = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tok0 = blockIdx.x * a.nt, row0 = blockIdx.y * 128;
+    const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / 32;
+    const uint32_t s0 = blockIdx.z * a.kps, s1 = min(kst, s0 + a.kps);
+    const uint32_t nst = s1 > s0 ? s1 - s0 : 0;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < S; ++i) {
+            mbar_init(&full_t[i], 1);
+            mbar_init(&full_s[i], 128);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(accb, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, G.tmem_cols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tbase = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tc::tma_prefetch_desc(&map_w);
+            tc::tma_prefetch_desc(&map_a);
+            uint32_t issued = 0;
+            for (uint32_t i = 0; i < nst; ++i) {
+                const uint32_t slot = i % S;
+                if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
+                uint8_t *st = smem + slot * G.stage_bytes;
+                mbar_arrive_expect_tx(&full_t[slot], kTileA + a.nt * 128);
+                const int32_t kx = (int32_t)((s0 + i) * 128);
+                tc::tma_load_2d(st, &map_w, kx, (int32_t)row0, &full_t[slot]);
+                tc::tma_load_2d(st + G.b_off, &map_a, kx, (int32_t)tok0, &full_t[slot]);
+                issued = i + 1;
+            }
+            // Never leave with copies in flight: wait for the last use of each slot.
+            for (uint32_t i = issued > S ? issued - S : 0; i < issued; ++i)
+                for (uint32_t it = 0; it < kSpinLimit && !mbar_try_wait(&full_t[i % S], (i / S) & 1); ++it) {
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_mxf4(a.nt);
+            for (uint32_t i = 0; i < nst; ++i) {
+                const uint32_t slot = i % S, par = (i / S) & 1;
+                if (!wait_or_abort(&full_t[slot], par, abort) || !wait_or_abort(&full_s[slot], par, abort)) break;
+                tc::fence_after_sync();
+                const uint8_t *st = smem + slot * G.stage_bytes;
+                const uint32_t sa_col = tbase + G.sfa_col0 + slot * 8;
+                const uint32_t sb_col = tbase + G.sfb_col0 + slot * 8 * G.sfb_atoms;
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {  // K = 128 halves of the stage
+                    tc::utccp_scale_atom(sa_col + 4 * h, tc::desc_scale_atom(smem_u32(st + G.sfa_off + h * 512)));
+                    for (uint32_t q = 0; q < G.sfb_atoms; ++q)
+                        tc::utccp_scale_atom(sb_col + h * 4 * G.sfb_atoms + 4 * q,
+                                             tc::desc_scale_atom(smem_u32(st + G.sfb_off + (q * 2 + h) * 512)));
+                }
+                const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + G.b_off);
+#pragma unroll
+                for (uint32_t kk = 0; kk < 4; ++kk) {
+                    const uint32_t h = kk >> 1, sid = (kk & 1) * 2;
+                    tc::mma_mxf4(tbase, tc::desc_sw128(a_addr + 32 * kk), tc::desc_sw128(b_addr + 32 * kk), idesc,
+                                 (sa_col + 4 * h) | (sid << 30), (sb_col + h * 4 * G.sfb_atoms) | (sid << 30),
+                                 (i | kk) != 0);
+                }
+                tc::commit(&empty[slot]);
+            }
+            tc::commit(accb);  // also on abort: the epilogue then knows no MMA is in flight
+        }
+    } else {
+        const uint32_t t = threadIdx.x - 64;  // 0..127
+        for (uint32_t i = 0; i < nst; ++i) {
+            const uint32_t slot = i % S;
+            if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
+            uint8_t *st = smem + slot * G.stage_bytes;
+            const uint32_t kb0 = (s0 + i) * 8;
+            const uint2 wa = load_scales8(a.sw, row0 + t, a.n, kb0, kbt);
+            *reinterpret_cast<uint32_t *>(st + G.sfa_off + tc::scale_atom_off(t, 0)) = wa.x;
+            *reinterpret_cast<uint32_t *>(st + G.sfa_off + 512 + tc::scale_atom_off(t, 0)) = wa.y;
+            for (uint32_t q = 0; q < G.sfb_atoms; ++q) {
+                const uint32_t r = t + 128 * q;
+                const uint2 wb = r < a.nt ? load_scales8(a.sa, tok0 + r, a.m, kb0, kbt) : make_uint2(0, 0);
+                *reinterpret_cast<uint32_t *>(st + G.sfb_off + (q * 2) * 512 + tc::scale_atom_off(t, 0)) = wb.x;
+                *reinterpret_cast<uint32_t *>(st + G.sfb_off + (q * 2 + 1) * 512 + tc::scale_atom_off(t, 0)) = wb.y;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&full_s[slot]);
+        }
+        // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31
+        bool ok = wait_or_abort(accb, 0, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        tc::fence_after_sync();
+        if (ok) {
+            const uint32_t q = (uint32_t)warp & 3, row = row0 + 32 * q + lane;
+            const bool row_ok = row < a.n;
+            for (uint32_t c0 = 0; c0 < a.nt; c0 += 8) {
+                float v[8];
+                tc::tmem_ld_x8(tbase + ((32 * q) << 16) + c0, v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (uint32_t j = 0; j < 8; ++j) {
+                    const uint32_t tok = tok0 + c0 + j;
+                    if (!row_ok || tok >= a.m) continue;
+                    const size_t o = (size_t)tok * a.n + row;
+                    if (a.mode == OUT_BF16)
+                        reinterpret_cast<uint16_t *>(a.d)[o] = f32_to_bf16_bits(v[j]);
+                    else if (a.mode == OUT_F32)
+                        reinterpret_cast<float *>(a.d)[o] = v[j];
+                    else
+                        atomicAdd(reinterpret_cast<float *>(a.d) + o, v[j]);
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tbase, G.tmem_cols);
+    }
+}
+
+__global__ void f32_to_bf16_kernel(const float *__restrict__ x, uint16_t *__restrict__ y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = f32_to_bf16_bits(x[i]);
+}
+
+// Known-answer kernel of the reference's fp4_mma_allones: A = B = 0x22 bytes
+// (every E2M1 value 1.0), every scale 127 (2^0), K = 64 -> every D = 64.0.
+// Operands are written straight into shared memory (no TMA), one MMA.
+__global__ void __launch_bounds__(128, 1) allones_kernel(float *out) {
+    __shared__ __align__(1024) uint8_t tile_a[128 * 128];
+    __shared__ __align__(1024) uint8_t tile_b[8 * 128];
+    __shared__ __align__(128) uint8_t atom_a[512], atom_b[512];
+    __shared__ __align__(8) uint64_t done;
+    __shared__ uint32_t tslot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t i = threadIdx.x; i < sizeof(tile_a) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(tile_a)[i] = 0x22222222u;
+    for (uint32_t i = threadIdx.x; i < sizeof(tile_b) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(tile_b)[i] = 0x22222222u;
+    reinterpret_cast<uint32_t *>(atom_a)[threadIdx.x] = 0x7F7F7F7Fu;
+    reinterpret_cast<uint32_t *>(atom_b)[threadIdx.x] = 0x7F7F7F7Fu;
+    if (threadIdx.x == 0) {
+        mbar_init(&done, 1);
+        fence_mbar_init();
+    }
+    fence_proxy_async_smem();
+    if (warp == 0) {
+        tc::tmem_alloc(&tslot, 32);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tbase = tslot;
+    if (threadIdx.x == 0) {
+        tc::utccp_scale_atom(tbase + 8, tc::desc_scale_atom(smem_u32(atom_a)));
+        tc::utccp_scale_atom(tbase + 12, tc::desc_scale_atom(smem_u32(atom_b)));
+        tc::mma_mxf4(tbase, tc::desc_sw128(smem_u32(tile_a)), tc::desc_sw128(smem_u32(tile_b)), tc::idesc_mxf4(8),
+                     tbase + 8, tbase + 12, 0);
+        tc::commit(&done);
+    }
+    bool ok = true;
+    for (uint32_t it = 0; !mbar_try_wait(&done, 0); ++it)
+        if (it >= kSpinLimit) {
+            ok = false;
+            raise_device_error(DEVERR_MBAR_TIMEOUT);
+            break;
+        }
+    ok = __all_sync(0xffffffffu, ok);
+    tc::fence_after_sync();
+    if (ok) {
+        float v[8];
+        tc::tmem_ld_x8(tbase + ((32 * warp) << 16), v);
+        tc::tmem_wait_ld();
+        const uint32_t r = 32 * warp + lane;
+        if (r < 16)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out[r * 8 + j] = v[j];
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tbase, 32);
+    }
+}
+
+struct Plan {
+    uint32_t nt, m_tiles, n_tiles, kst, kps, splits;
+    Geo g;
+};
+
+inline Plan plan(uint32_t m, uint32_t n, uint32_t k) {
+    Plan p;
+    p.nt = m >= 256 ? 256 : (m + 7) / 8 * 8;
+    p.m_tiles = (m + p.nt - 1) / p.nt;
+    p.n_tiles = (n + 127) / 128;
+    p.kst = (k + kStageK - 1) / kStageK;
+    const uint32_t tiles = p.m_tiles * p.n_tiles, sms = (uint32_t)num_sms();
+    uint32_t splits = 1;
+    if (tiles < sms) splits = std::min(p.kst, (sms + tiles - 1) / tiles);
+    p.kps = (p.kst + splits - 1) / splits;
+    p.splits = (p.kst + p.kps - 1) / p.kps;
+    p.g = geometry(p.nt);
+    return p;
+}
+
+int validate(uint32_t m, uint32_t n, uint32_t k, const void *a, const void *sa, const void *w, const void *sw,
+             const void *d) {
+    FP4X_REQUIRE(m > 0 && n > 0 && k > 0, "fp4_mma: empty shape m=%u n=%u k=%u", m, n, k);
+    FP4X_REQUIRE(k % 64 == 0, "fp4_mma: k=%u must be a multiple of 64", k);
+    FP4X_REQUIRE(a && sa && w && sw && d, "fp4_mma: null pointer");
+    FP4X_REQUIRE(aligned16(a) && aligned16(w), "fp4_mma: packed operands must be 16-byte aligned");
+    FP4X_REQUIRE(m <= (1u << 24) && n <= (1u << 24) && k <= (1u << 20), "fp4_mma: shape too large");
+    return FP4X_OK;
+}
+
+int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa,
+           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p) {
+    CUtensorMap map_w, map_a;
+    if (!tc::make_map_sw128(&map_w, w, k / 2, n, 128) || !tc::make_map_sw128(&map_a, a, k / 2, m, p.nt)) {
+        set_error("fp4_mma: cuTensorMapEncodeTiled failed (m=%u n=%u k=%u)", m, n, k);
+        return FP4X_ECUDA;
+    }
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(mxf4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kSmemLimit);
+    });
+    if (attr_err != cudaSuccess) {
+        set_error("fp4_mma: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+        return FP4X_ECUDA;
+    }
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode};
+    mxf4_gemm_kernel<<<dim3(p.m_tiles, p.n_tiles, p.splits), kThreads, p.g.smem, s>>>(map_w, map_a, args);
+    return check_launch("fp4_mma");
+}
+
+}  // namespace mma
+}  // namespace fp4x
+
+using namespace fp4x;
+
+extern "C" size_t fp4_mma_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
+    if (m == 0 || n == 0 || k == 0) return 0;
+    const mma::Plan p = mma::plan(m, n, k);
+    return p.splits > 1 ? (size_t)m * n * sizeof(float) : 0;
+}
+
+extern "C" int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                       const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, uint16_t *d_bf16,
+                       void *workspace, size_t workspace_bytes) {
+    if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d_bf16)) return e;
+    const mma::Plan p = mma::plan(m, n, k);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p.splits == 1) return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d_bf16, mma::OUT_BF16, p);
+    const size_t need = (size_t)m * n * sizeof(float);
+    FP4X_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+                 "fp4_mma: split-K needs a 16-byte aligned workspace of %zu bytes (fp4_mma_workspace_size)", need);
+    if (cudaMemsetAsync(workspace, 0, need, s) != cudaSuccess) return check_launch("fp4_mma workspace clear");
+    if (int e = mma::launch(s, m, n, k, a, a_scales, w, w_scales, workspace, mma::OUT_RED_F32, p)) return e;
+    const size_t total = (size_t)m * n;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, 4 * (size_t)num_sms());
+    mma::f32_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float *>(workspace), d_bf16, total);
+    return check_launch("fp4_mma convert");
+}
+
+extern "C" int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                           const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float *d) {
+    if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d)) return e;
+    const mma::Plan p = mma::plan(m, n, k);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p.splits == 1) return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p);
+    if (cudaMemsetAsync(d, 0, (size_t)m * n * sizeof(float), s) != cudaSuccess) return check_launch("fp4_mma_f32 clear");
+    return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_RED_F32, p);
+}
+
+extern "C" int fp4_mma_allones(fp4x_stream_t stream, float *out) {
+    FP4X_REQUIRE(out, "fp4_mma_allones: null pointer");
+    mma::allones_kernel<<<1, 128, 0, (cudaStream_t)stream>>>(out);
+    return check_launch("fp4_mma_allones");
+}

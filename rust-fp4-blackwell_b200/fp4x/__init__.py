@@ -51,6 +51,10 @@ SIGNATURES = {
     "fp4_gemv": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp]),
     "fp4_gemv_ref": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp]),
     "fp4_gemv_f32x": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp]),
+    "fp4_mma_workspace_size": (_sz, [_u32, _u32, _u32]),
+    "fp4_mma": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fp4_mma_f32": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "fp4_mma_allones": (C.c_int, [_vp, _vp]),
     "llama_rmsnorm": (C.c_int, [_vp, _u32, _f32, _vp, _vp, _vp]),
     "llama_rope": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp]),
     "llama_rope_tables": (C.c_int, [_vp, _u32, _u32, C.c_double, _vp, _vp]),

@@ -85,6 +85,31 @@ def gemv_ref(words: torch.Tensor, scales: torch.Tensor, x: torch.Tensor):
     return y
 
 
+def mma(a: torch.Tensor, sa: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, out_dtype=torch.bfloat16):
+    """d[m][n] = A W^T for MXFP4 A [m][k/2] (+ E8M0 scales [m][k/32]) and W [n][k/2]
+    (+ [n][k/32]) on tcgen05.mma.kind::mxf4; bf16 (fp4_mma) or fp32 (fp4_mma_f32) out."""
+    m, n, k = a.shape[0], w.shape[0], a.shape[1] * 2
+    if w.shape[1] * 2 != k or sa.shape != (m, k // 32) or sw.shape != (n, k // 32):
+        raise ValueError("fp4 mma: operand shapes disagree")
+    d = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    if out_dtype == torch.float32:
+        check(lib().fp4_mma_f32(_stream(), m, n, k, _ptr(a), _ptr(sa), _ptr(w), _ptr(sw), _ptr(d)))
+        return d
+    if out_dtype != torch.bfloat16:
+        raise ValueError(out_dtype)
+    ws_bytes = lib().fp4_mma_workspace_size(m, n, k)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=a.device)
+    check(lib().fp4_mma(_stream(), m, n, k, _ptr(a), _ptr(sa), _ptr(w), _ptr(sw), _ptr(d), _ptr(ws), ws_bytes))
+    return d
+
+
+def mma_allones(device="cuda"):
+    """The reference's all-ones known-answer test on tcgen05: [16][8], every value 64.0."""
+    out = torch.full((16, 8), -1.0, dtype=torch.float32, device=device)
+    check(lib().fp4_mma_allones(_stream(), _ptr(out)))
+    return out
+
+
 def rmsnorm(x, w, eps=1e-5):
     y = torch.empty_like(x)
     check(lib().llama_rmsnorm(_stream(), x.numel(), eps, _ptr(x), _ptr(w), _ptr(y)))
