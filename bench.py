@@ -131,6 +131,14 @@ class ClockSampler:
         return out
 
 
+DTYPES = {
+    "tensor": "e2m1xe8m0 weights x 8-term e2m1xe8m0 activation on tcgen05 kind::mxf4 (exact products, "
+              "fp32 accumulate), bf16 KV",
+    "persistent": "e2m1xe8m0 weights, f32 activations (f16 hi/lo mma.sync operands), bf16 KV",
+    "graph": "e2m1xe8m0 weights, f32 activations (f16 hi/lo mma.sync operands), bf16 KV",
+}
+
+
 def cpu_baseline_port(cfg, budget_s=20.0, threads=0):
     """Oracle forward (reference CPU loops, OpenMP over rows) on a bounded sample."""
     import oracle
@@ -331,7 +339,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_tok * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "e2m1xe8m0 weights, f32 activations (f16 hi/lo tensor-core operands), bf16 KV",
+        "vs_baseline": None, "dtype": DTYPES[model_path],
         "data": "synthetic (seeded N(0,0.02) weights -> MXFP4, seeded uniform prompt ids)",
         "config": {"workload": "config1: TinyLlama-shape MXFP4 decode, bs1, 16-token prompt, greedy",
                    "n_layers": 22, "dim": 2048, "ffn": 5632, "heads": "32q/4kv", "head_dim": 64, "vocab": 32000,

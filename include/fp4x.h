@@ -227,9 +227,10 @@ FP4X_API int llama_decode_step(fp4x_llama_model *m, fp4x_stream_t stream);
 /* n tokens of the device-resident loop in one call (one launch on the
  * persistent path). */
 FP4X_API int llama_decode_steps(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t n);
-/* Decode path: 1 = persistent kernel (one cooperative launch runs many tokens;
- * default when the shape fits), 0 = CUDA graph of fused per-layer kernels.
- * The environment variable FP4X_DECODE_PATH=graph selects 0 at creation. */
+/* Decode path: 2 = persistent kernel on tcgen05 MXFP4 MMAs (one cooperative
+ * launch runs many tokens; default when the shape fits), 1 = persistent kernel
+ * with CUDA-core MXFP4 decode, 0 = CUDA graph of fused per-layer kernels.
+ * FP4X_DECODE_PATH=graph|persistent selects 0|1 at creation. */
 FP4X_API int llama_model_set_path(fp4x_llama_model *m, int path);
 FP4X_API int llama_model_get_path(const fp4x_llama_model *m);
 /* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-587, EOS

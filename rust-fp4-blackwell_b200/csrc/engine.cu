@@ -74,9 +74,12 @@ struct fp4x_llama_model {
     float *norms = nullptr;        // attn norms [L][dim] then ffn norms [L][dim]
     uint16_t *kv = nullptr;        // K [L][max_seq][kvd] then V [L][max_seq][kvd]
     fp4x::persist::Engine *pe = nullptr;  // persistent decode kernel (null: unsupported shape)
-    int path = 0;                  // 0: CUDA graph of fused kernels, 1: persistent kernel
+    fp4x::ptc::Engine *pt = nullptr;      // tensor-core persistent decode kernel (null: unsupported)
+    int path = 0;                  // 0: CUDA graph of fused kernels, 1: persistent kernel (CUDA-core
+                                   // MXFP4 decode), 2: persistent kernel on tcgen05 MMAs
     int64_t hpos = -1;             // host view of the device-resident position (-1: unknown)
     char persist_why[256] = "";    // why the persistent kernel is unavailable, if it is
+    char tc_why[256] = "";         // why the tensor-core kernel is unavailable, if it is
 };
 
 namespace fp4x {
@@ -366,8 +369,20 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
         } else {
             rc = prc;
         }
+        if (!rc) {
+            const int trc = ptc::build(in, m->cap_stream, &m->pt);
+            if (trc == FP4X_OK) {
+                m->path = 2;
+            } else if (trc == FP4X_EUNSUPPORTED) {
+                m->pt = nullptr;
+                snprintf(m->tc_why, sizeof(m->tc_why), "%s", fp4x_last_error());
+            } else {
+                rc = trc;
+            }
+        }
         const char *env = getenv("FP4X_DECODE_PATH");
         if (env && strcmp(env, "graph") == 0) m->path = 0;
+        if (env && strcmp(env, "persistent") == 0 && m->pe) m->path = 1;
     }
     if (rc) return fail(rc);
     *out = m;
@@ -379,7 +394,9 @@ int run_tokens(fp4x_llama_model *m, cudaStream_t st, uint32_t n) {
     FP4X_REQUIRE(m->hpos >= 0, "decode: no position set (call llama_forward or llama_generate first)");
     FP4X_REQUIRE((uint64_t)m->hpos + n <= m->cfg.max_seq, "decode: position %lld + %u tokens exceeds max_seq %u",
                  (long long)m->hpos, n, m->cfg.max_seq);
-    if (m->path == 1) {
+    if (m->path == 2) {
+        FP4X_TRY(ptc::launch(m->pt, st, n));
+    } else if (m->path == 1) {
         FP4X_TRY(persist::launch(m->pe, st, n));
     } else {
         for (uint32_t i = 0; i < n; ++i) FP4X_CUDA(cudaGraphLaunch(m->exec, st));
@@ -416,6 +433,7 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
         cudaStreamDestroy(m->cap_stream);
     }
     persist::destroy(m->pe);
+    ptc::destroy(m->pt);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return FP4X_OK;
@@ -440,9 +458,13 @@ extern "C" int llama_decode_steps(fp4x_llama_model *m, fp4x_stream_t stream, uin
 }
 
 extern "C" int llama_model_set_path(fp4x_llama_model *m, int path) {
-    FP4X_REQUIRE(m && (path == 0 || path == 1), "llama_model_set_path: bad argument");
+    FP4X_REQUIRE(m && path >= 0 && path <= 2, "llama_model_set_path: bad argument");
     if (path == 1 && !m->pe) {
         set_error("llama_model_set_path: the persistent kernel is unavailable: %s", m->persist_why);
+        return FP4X_EUNSUPPORTED;
+    }
+    if (path == 2 && !m->pt) {
+        set_error("llama_model_set_path: the tensor-core kernel is unavailable: %s", m->tc_why);
         return FP4X_EUNSUPPORTED;
     }
     m->path = path;

@@ -7,4 +7,5 @@
 #include "attention.cu"
 #include "mma.cu"
 #include "persist.cu"
+#include "persist_tc.cu"
 #include "engine.cu"

@@ -89,8 +89,9 @@ __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, float (&v)[8]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- MMA issue (one thread)
+// (no memory clobber: ordering against the mbarrier waits comes from volatile-asm order)
 __device__ __forceinline__ void utccp_scale_atom(uint32_t taddr, uint64_t sdesc) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc));
 }
 
 // D[tmem_d] (+)= A * B^T with block scales; scale ids ride in bits 30..31 of the
@@ -102,8 +103,7 @@ __device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %6, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(id), "r"(tsfa), "r"(tsfb), "r"(accumulate)
-        : "memory");
+        "l"(adesc), "l"(bdesc), "r"(id), "r"(tsfa), "r"(tsfb), "r"(accumulate));
 }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread is done.

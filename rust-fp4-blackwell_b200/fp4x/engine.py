@@ -116,10 +116,10 @@ class Model:
 
     @property
     def path(self) -> str:
-        return {0: "graph", 1: "persistent"}[self.L.llama_model_get_path(self._h)]
+        return {0: "graph", 1: "persistent", 2: "tensor"}[self.L.llama_model_get_path(self._h)]
 
     def set_path(self, path: str):
-        check(self.L.llama_model_set_path(self._h, {"graph": 0, "persistent": 1}[path]))
+        check(self.L.llama_model_set_path(self._h, {"graph": 0, "persistent": 1, "tensor": 2}[path]))
 
     def generate(self, prompt, n_gen: int):
         prompt = np.ascontiguousarray(prompt, np.uint32)

@@ -62,7 +62,10 @@ def test_engine_weights_bit_exact(cfg):
     ref.close()
 
 
-@pytest.mark.parametrize("path", ["graph", "persistent"])
+PATHS = ["graph", "persistent", "tensor"]
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
 def test_engine_forward_vs_oracle(cfg, path):
     ref = oracle.Model(cfg)
@@ -77,7 +80,7 @@ def test_engine_forward_vs_oracle(cfg, path):
     ref.close()
 
 
-@pytest.mark.parametrize("path", ["graph", "persistent"])
+@pytest.mark.parametrize("path", PATHS)
 def test_engine_generate_equals_forward_loop(path):
     prompt = oracle.uniform_ids(8, TINY["vocab"], 5)
     with engine.Model(TINY) as m:
@@ -98,7 +101,7 @@ def test_engine_generate_equals_forward_loop(path):
         torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("path", ["graph", "persistent"])
+@pytest.mark.parametrize("path", PATHS)
 def test_engine_generate_matches_oracle_tiny(path):
     prompt = oracle.uniform_ids(3, TINY["vocab"], 6)
     ref = oracle.Model(TINY)
@@ -110,13 +113,15 @@ def test_engine_generate_matches_oracle_tiny(path):
     np.testing.assert_array_equal(got, want)
 
 
-def test_engine_default_path_is_persistent():
+def test_engine_default_path_is_tensor():
     with engine.Model(TINY) as m:
-        assert m.path == "persistent"
+        assert m.path == "tensor"
 
 
-def test_engine_decode_steps_bounded_by_max_seq():
+@pytest.mark.parametrize("path", PATHS)
+def test_engine_decode_steps_bounded_by_max_seq(path):
     with engine.Model(TINY) as m:
+        m.set_path(path)
         m.generate(oracle.uniform_ids(1, TINY["vocab"], 4), 1)  # device position 4
         with pytest.raises(Exception):
             m.decode_steps(TINY["max_seq"])  # would run past the cache
@@ -130,7 +135,8 @@ def test_engine_rejects_bad_config():
         engine.Model(bad)
 
 
-def test_engine_tinyllama_config1():
+@pytest.mark.parametrize("path", ["persistent", "tensor"])
+def test_engine_tinyllama_config1(path):
     """BASELINE config 1: 22 layers, d 2048, ffn 5632, 32q/4kv, hd 64, V 32000, theta 1e4;
     16 seeded prompt ids, 128 greedy tokens.  Weights bit-exact (sampled tensors),
     logits within 1e-2 at every position, the same greedy tokens (teacher forcing
@@ -139,7 +145,7 @@ def test_engine_tinyllama_config1():
     prompt = oracle.uniform_ids(oracle.hash64(cfg["seed"], 2), cfg["vocab"], 16)
     ref = oracle.Model(cfg)
     with engine.Model(cfg) as m:
-        assert m.path == "persistent"
+        m.set_path(path)
         for tid in (1, 16, 16 + 2, 16 + 8 * 21 + 6):
             n, k = shape_of(cfg, tid)
             gp, gs = m.export_tensor(tid)
