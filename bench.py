@@ -131,6 +131,10 @@ class ClockSampler:
         return out
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per token from one ncu capture of the
+# timed launch (profiles/decode_tc_kernel_tinyllama_bs1.md); None where not captured.
+TRAFFIC_PER_TOKEN = {"tensor": (11.331308e9 + 13.233920e6) / 20}
+
 DTYPES = {
     "tensor": "e2m1xe8m0 weights x 8-term e2m1xe8m0 activation on tcgen05 kind::mxf4 (exact products, "
               "fp32 accumulate), bf16 KV",
@@ -204,6 +208,76 @@ def run_reference(args):
     return 0
 
 
+C3_LINEARS = {"qkv": (2560, 2048), "o": (2048, 2048), "gate_up": (11264, 2048), "down": (2048, 5632),
+              "lm_head": (32000, 2048)}
+
+
+def run_config3(args):
+    """BASELINE config 3: fp4_mma (tcgen05 kind::mxf4) on the TinyLlama linears x M tokens
+    (16/64/256 decode batches, 512-token prefill), MXFP4 N(0,1) activations, fp32
+    accumulate, bf16 out.  Each (M, linear) is a CUDA graph of calls over rotated weight
+    copies (> 300 MB, so weights come from HBM), timed with CUDA events."""
+    import torch
+    from fp4x import check, lib, ops
+    L = lib()
+    peak, peak_kind = hbm_peak()
+    ms = [int(x) for x in args.c3_m.split(",")]
+    names = args.c3_linears.split(",")
+    rows, tot_flop, tot_us = [], 0.0, 0.0
+    for m in ms:
+        for name in names:
+            n, k = C3_LINEARS[name]
+            wbytes = n * k // 2 + n * k // 32
+            copies = max(2, -(-(300 << 20) // wbytes))
+            ws = [ops.init_mxfp4(n, k, seed=100 + i) for i in range(copies)]
+            a, sa = ops.init_mxfp4(m, k, seed=7, sigma=1.0)
+            d = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+            wsb = L.fp4_mma_workspace_size(m, n, k)
+            wsp = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+
+            def call(p, sc):
+                check(L.fp4_mma(s.cuda_stream, m, n, k, a.data_ptr(), sa.data_ptr(), p.data_ptr(), sc.data_ptr(),
+                                d.data_ptr(), wsp.data_ptr(), wsb))
+            with torch.cuda.stream(s):
+                call(*ws[0])
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for p, sc in ws:
+                    call(p, sc)
+            for _ in range(args.warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            st = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
+            byts = wbytes + m * k // 2 + m * k // 32 + m * n * 2
+            flop = 2.0 * m * n * k
+            rows.append({"m": m, "linear": name, "n": n, "k": k, "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+                         "tflops": round(flop / us / 1e6, 1), "split_k": wsb > 0})
+            if m == ms[-1]:
+                tot_flop += flop
+                tot_us += us
+            del ws, g
+            torch.cuda.empty_cache()
+    line = {"metric": f"fp4_mma config3: TinyLlama linears at M={ms[-1]} tokens", "value": tot_flop / tot_us / 1e6,
+            "unit": "TFLOP/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "e2m1 x e2m1 (E8M0 block-32 scales), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations -> MXFP4)",
+            "config": {"workload": "config3", "tokens": ms, "linears": names,
+                       "l2": "rotated weight copies > 300 MB per graph"},
+            "hbm_peak_gbs": peak, "peak_kind": peak_kind, "table": rows}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def gemv_config0(torch, peak):
     """Config 0 GEMV (fp4_gemv through the C ABI) over 64 rotated weight copies,
     captured in one CUDA graph (no host launch gaps), CUDA-event timed."""
@@ -251,10 +325,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--config3", action="store_true", help="fp4_mma sweep of BASELINE config 3 instead of decode")
+    ap.add_argument("--c3-m", default="16,64,256,512")
+    ap.add_argument("--c3-linears", default=",".join(C3_LINEARS))
     args = ap.parse_args()
     assert args.warmup >= 3, "timing rules: at least 3 warm-up steps"
     if args.impl == "reference":
         return run_reference(args)
+    if args.config3:
+        return run_config3(args)
 
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -348,7 +427,8 @@ def main():
                    "l2": "no flush: 549.5 MB of weights per step > 126 MB L2"},
         "roofline": {"bound": "hbm", "kernel": f"decode token ({model_path} path)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "bytes_per_launch": wbytes, "peak_kind": peak_kind},
+                     "traffic": TRAFFIC_PER_TOKEN.get(model_path), "bytes_per_launch": wbytes,
+                     "peak_kind": peak_kind, "traffic_source": "ncu dram bytes of a 20-token launch / 20"},
         "gemv": gemv,
         "cpu_baseline": cpu,
         "e2e": e2e,

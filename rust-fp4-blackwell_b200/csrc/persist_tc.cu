@@ -255,20 +255,76 @@ __device__ __forceinline__ uint32_t pack_e2m1x8(const float (&y)[8]) {
     return w;
 }
 
-// 8-term MXFP4 decomposition of v[0, K) (K % 32 == 0).  B receives the terms as
-// operand rows 0..7 ([K/32][8][16 B], low nibble = lower k); sfb their E8M0
-// scales in 128-byte atoms (row t at 16t): block b at atom b/4 byte b%4
-// (natural), or at atom b/2 bytes 2(b%2) and 2(b%2)+1 (pairs, for K32 blocks).
-// Scale schedule per 32-block with maximum a: e1 = the smallest exponent with
-// a <= 6 * 2^e1, then e1 - 2, then 3 less per term.  Rounding to nearest keeps
-// the residual after term 1 within 2^e1 and after each later term within half
-// its scale, so every term's values stay inside +-6 and the 8-term sum equals v
-// to 2^(e1-21) (~1.6e-7 of the block maximum); every step is exact in fp32.
-// One thread owns 8 consecutive values (one packed word per term).
+// 8-term MXFP4 decomposition (operand rows 0..7 of B, [K/32][8][16 B], low nibble
+// = lower k) of the 8 values x[] that this thread owns: word w (0..3) of 32-block b.
+// The 4 threads of a block must sit in adjacent lanes (4b'..4b'+3 of the warp) and
+// every lane of the warp must call (valid = false for padding lanes).  Scales go to
+// sfb in 128-byte atoms (row t at 16t): block b at atom b/4 byte b%4 (natural), or
+// at atom b/2 bytes 2(b%2), 2(b%2)+1 (pairs, for K32 blocks).
+// Scale schedule per block with maximum a: e1 = the smallest exponent with
+// a <= 6 * 2^e1, then e1 - 2, then 3 less per term.  Rounding to nearest keeps the
+// residual after term 1 within 2^e1 and after each later term within half its
+// scale, so every term stays inside +-6 and the 8-term sum equals the input to
+// 2^(e1-21) (~1.6e-7 of the block maximum); every step is exact in fp32.
+__device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint32_t w, bool valid, uint8_t *B,
+                                                uint8_t *sfb, bool pairs) {
+    float a = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(x[j]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    const uint32_t bits = __float_as_uint(a);
+    int e1 = (int)((bits >> 23) & 0xFFu) - 127;
+    e1 = (bits & 0x7FFFFFu) <= 0x400000u ? e1 - 2 : e1 - 1;
+    uint32_t words[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int e = max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t));
+        const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+        const float s = __uint_as_float((uint32_t)(127 + e) << 23);
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = x[j] * inv;
+        words[t] = pack_e2m1x8(y);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t hv = e2m1x2_to_f16x2((words[t] >> (8 * j)) & 0xFFu);
+            const __half2 q = *reinterpret_cast<const __half2 *>(&hv);
+            x[2 * j] = fmaf(-__low2float(q), s, x[2 * j]);
+            x[2 * j + 1] = fmaf(-__high2float(q), s, x[2 * j + 1]);
+        }
+    }
+    if (!valid) return;
+    // term order rotated by block: the 8 blocks of a warp (128 bytes apart) then hit
+    // 8 different bank groups instead of one
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const uint32_t t = (r + b) & 7u;
+        uint32_t wv = words[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) wv = t == (uint32_t)q ? words[q] : wv;
+        *reinterpret_cast<uint32_t *>(B + b * 128 + t * 16 + w * 4) = wv;
+    }
+    if (w == 0) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint8_t sb = (uint8_t)(max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t)) + 127);
+            if (!pairs) {
+                sfb[(b >> 2) * 128 + t * 16 + (b & 3)] = sb;
+            } else {
+                uint8_t *q2 = sfb + (b >> 1) * 128 + t * 16 + 2 * (b & 1);
+                q2[0] = sb;
+                q2[1] = sb;
+            }
+        }
+    }
+}
+
+// Decomposition of v[0, K) in shared memory (K % 32 == 0), one word per thread.
 __device__ void decompose8(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb, bool pairs) {
     const uint32_t nw = K / 8, lane = threadIdx.x & 31;
     for (uint32_t base = threadIdx.x - lane; base < nw; base += kCons) {
-        const uint32_t i = base + lane, b = i >> 2, w = i & 3;
+        const uint32_t i = base + lane;
         const bool valid = i < nw;  // the 4 words of a block are valid together
         float x[8];
         if (valid) {
@@ -279,71 +335,67 @@ __device__ void decompose8(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb,
 #pragma unroll
             for (int j = 0; j < 8; ++j) x[j] = 0.0f;
         }
-        float a = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(x[j]));
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-        const uint32_t bits = __float_as_uint(a);
-        int e1 = (int)((bits >> 23) & 0xFFu) - 127;
-        e1 = (bits & 0x7FFFFFu) <= 0x400000u ? e1 - 2 : e1 - 1;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const int e = max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t));
-            const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
-            const float s = __uint_as_float((uint32_t)(127 + e) << 23);
-            float y[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) y[j] = x[j] * inv;
-            const uint32_t word = pack_e2m1x8(y);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t hv = e2m1x2_to_f16x2((word >> (8 * j)) & 0xFFu);
-                const __half2 q = *reinterpret_cast<const __half2 *>(&hv);
-                x[2 * j] = fmaf(-__low2float(q), s, x[2 * j]);
-                x[2 * j + 1] = fmaf(-__high2float(q), s, x[2 * j + 1]);
-            }
-            if (valid) {
-                *reinterpret_cast<uint32_t *>(B + b * 128 + t * 16 + w * 4) = word;
-                if (w == 0) {
-                    const uint8_t sb = (uint8_t)(e + 127);
-                    if (!pairs) {
-                        sfb[(b >> 2) * 128 + t * 16 + (b & 3)] = sb;
-                    } else {
-                        uint8_t *q2 = sfb + (b >> 1) * 128 + t * 16 + 2 * (b & 1);
-                        q2[0] = sb;
-                        q2[1] = sb;
-                    }
-                }
-            }
-        }
+        decompose_word8(x, i >> 2, i & 3, valid, B, sfb, pairs);
     }
 }
 
-// RMSNorm input staging: xv = (src * rms) * w, returns nothing (xv in smem).
-// MODE 0: src = X, 1: src = X + Y, 2: src = bf16 embedding row (CTA 0 writes it to X).
+// RMSNorm + decomposition in registers: thread i owns values [8i, 8i+8) (and
+// [8(i+kCons), ...) when dim > 8 * kCons).  xn = (src * rms) * w
+// (llama_run:79-116), src = X (MODE 0), X + Y (1) or the bf16 embedding row (2;
+// CTA 0 writes it to X).  With `decompose` false only the CTA-0 embedding copy runs.
 template <int MODE>
-__device__ void stage_norm(Ctx &c, const uint16_t *erow, const float *w) {
+__device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, bool decompose) {
     const Params &p = *c.p;
-    float *xv = reinterpret_cast<float *>(c.smem + c.L.xv);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float ss = 0.0f;
-    for (uint32_t i = threadIdx.x * 4; i < p.dim; i += kCons * 4) {
-        float4 r;
-        if (MODE == 2) {
-            const uint2 q = *reinterpret_cast<const uint2 *>(erow + i);
-            r = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
-                            __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
-            if (blockIdx.x == 0) *reinterpret_cast<float4 *>(p.X + i) = r;
-        } else {
-            r = __ldcg(reinterpret_cast<const float4 *>(p.X + i));
-            if (MODE == 1) {
-                const float4 y = __ldcg(reinterpret_cast<const float4 *>(p.Y + i));
-                r.x += y.x, r.y += y.y, r.z += y.z, r.w += y.w;
+    constexpr int R = 2;  // dim <= 16 * kCons
+    const uint32_t nw = p.dim / 8, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (!decompose) {
+        if (MODE == 2 && blockIdx.x == 0)
+            for (uint32_t i = threadIdx.x; i < nw; i += kCons) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(erow + 8 * i);
+                const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<float2 *>(p.X + 8 * i + 2 * j) =
+                        make_float2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xFFFF0000u));
             }
+        return;
+    }
+    float x[R][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const uint32_t i = threadIdx.x + r * kCons;
+        if (i < nw) {
+            if (MODE == 2) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(erow + 8 * i);
+                const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    x[r][2 * j] = __uint_as_float(u[j] << 16);
+                    x[r][2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+                }
+                if (blockIdx.x == 0) {
+                    *reinterpret_cast<float4 *>(p.X + 8 * i) = make_float4(x[r][0], x[r][1], x[r][2], x[r][3]);
+                    *reinterpret_cast<float4 *>(p.X + 8 * i + 4) = make_float4(x[r][4], x[r][5], x[r][6], x[r][7]);
+                }
+            } else {
+                const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(p.X + 8 * i));
+                const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(p.X + 8 * i + 4));
+                x[r][0] = a0.x, x[r][1] = a0.y, x[r][2] = a0.z, x[r][3] = a0.w;
+                x[r][4] = a1.x, x[r][5] = a1.y, x[r][6] = a1.z, x[r][7] = a1.w;
+                if (MODE == 1) {
+                    const float4 y0 = __ldcg(reinterpret_cast<const float4 *>(p.Y + 8 * i));
+                    const float4 y1 = __ldcg(reinterpret_cast<const float4 *>(p.Y + 8 * i + 4));
+                    x[r][0] += y0.x, x[r][1] += y0.y, x[r][2] += y0.z, x[r][3] += y0.w;
+                    x[r][4] += y1.x, x[r][5] += y1.y, x[r][6] += y1.z, x[r][7] += y1.w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += x[r][j] * x[r][j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[r][j] = 0.0f;
         }
-        *reinterpret_cast<float4 *>(xv + i) = r;
-        ss += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
     }
     ss = warp_sum(ss);
     if (lane == 0) c.red[warp] = ss;
@@ -351,14 +403,22 @@ __device__ void stage_norm(Ctx &c, const uint16_t *erow, const float *w) {
     float tot = 0.0f;
 #pragma unroll
     for (int i = 0; i < kCW; ++i) tot += c.red[i];
-    const float rms = 1.0f / sqrtf(tot / (float)p.dim + p.eps);  // llama_run:79-116
-    for (uint32_t i = threadIdx.x * 4; i < p.dim; i += kCons * 4) {
-        float4 r = *reinterpret_cast<const float4 *>(xv + i);
-        const float4 g = __ldg(reinterpret_cast<const float4 *>(w + i));
-        r.x = r.x * rms * g.x, r.y = r.y * rms * g.y, r.z = r.z * rms * g.z, r.w = r.w * rms * g.w;
-        *reinterpret_cast<float4 *>(xv + i) = r;
+    const float rms = 1.0f / sqrtf(tot / (float)p.dim + p.eps);
+    uint8_t *B = c.smem + c.L.bx, *sfb = c.smem + c.L.sfbx;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const uint32_t i = threadIdx.x + r * kCons;
+        if (i - lane >= nw) break;  // warp-uniform
+        const bool valid = i < nw;
+        if (valid) {
+            const float4 g0 = __ldg(reinterpret_cast<const float4 *>(w + 8 * i));
+            const float4 g1 = __ldg(reinterpret_cast<const float4 *>(w + 8 * i + 4));
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[r][j] = x[r][j] * rms * g[j];
+        }
+        decompose_word8(x[r], i >> 2, i & 3, valid, B, sfb, false);
     }
-    csync();
 }
 
 // ---------------------------------------------------------------- phases
@@ -368,12 +428,11 @@ __device__ void phase_qkv(Ctx &c, uint32_t l, uint32_t tok, uint32_t lay_count) 
     const Params &p = *c.p;
     const Sched &S = *c.S;
     if (l == 0)
-        stage_norm<2>(c, p.embed + (size_t)tok * p.dim, p.attn_norm);
+        norm_decompose<2>(c, p.embed + (size_t)tok * p.dim, p.attn_norm, S.n_a > 0);
     else
-        stage_norm<1>(c, nullptr, p.attn_norm + (size_t)l * p.dim);
+        norm_decompose<1>(c, nullptr, p.attn_norm + (size_t)l * p.dim, S.n_a > 0);
     CST(1);
     if (S.n_a == 0) return;
-    decompose8(reinterpret_cast<const float *>(c.smem + c.L.xv), p.dim, c.smem + c.L.bx, c.smem + c.L.sfbx, false);
     signal_operand(c, PH_QKV);
     CST(2);
     wait_acc(c, PH_QKV, lay_count & 1);
@@ -588,10 +647,9 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
         const uint32_t e0 = blockIdx.x * per, e1 = min(n, e0 + per);
         for (uint32_t e = e0 + threadIdx.x; e < e1; e += kCons) p.qkv[e] = 0.0f;
     }
-    stage_norm<0>(c, nullptr, p.ffn_norm + (size_t)l * p.dim);
+    norm_decompose<0>(c, nullptr, p.ffn_norm + (size_t)l * p.dim, S.U > 0);
     CST(12);
     if (S.U == 0) return;
-    decompose8(reinterpret_cast<const float *>(c.smem + c.L.xv), p.dim, c.smem + c.L.bx, c.smem + c.L.sfbx, false);
     signal_operand(c, PH_GU);
     CST(13);
     wait_acc(c, PH_GU, lay_count & 1);
@@ -630,13 +688,11 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
 __device__ void phase_lm(Ctx &c, uint32_t tok_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
-    stage_norm<1>(c, nullptr, p.final_norm);
+    norm_decompose<1>(c, nullptr, p.final_norm, S.n_l > 0);
     CST(1);
     float bv = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
     if (S.n_l > 0) {
-        decompose8(reinterpret_cast<const float *>(c.smem + c.L.xv), p.dim, c.smem + c.L.bx, c.smem + c.L.sfbx,
-                   false);
         signal_operand(c, PH_LM);
         CST(2);
         wait_acc(c, PH_LM, tok_count & 1);
