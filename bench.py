@@ -278,6 +278,77 @@ def run_config3(args):
     return 0
 
 
+def run_config2(args):
+    """batched bf16 flash-decode (llama_attn_decode_bf16 through the
+    C ABI): GQA 32q/4kv hd 64 and 32q/8kv hd 128, contexts 512..32768, batch 1/8/64.
+    Per shape a CUDA graph of calls over enough rotated KV caches to exceed 300 MB (or
+    one cache when it is larger), CUDA-event timed.  Bytes = K + V read + q + out."""
+    import torch
+    from fp4x import check, lib, ops
+    L = lib()
+    peak, peak_kind = hbm_peak()
+    shapes = [(32, 4, 64), (32, 8, 128)]
+    ctxs = [int(x) for x in args.c2_ctx.split(",")]
+    batches = [int(x) for x in args.c2_batch.split(",")]
+    rows = []
+    for (H, KV, hd) in shapes:
+        for B in batches:
+            for T in ctxs:
+                cache = B * T * KV * hd * 2 * 2
+                if cache > (24 << 30):
+                    continue
+                copies = max(1, min(16, -(-(300 << 20) // cache)))
+                kvs = []
+                for i in range(copies):
+                    kc = ops.fill_normal(B * T * KV * hd, seed=10 + 2 * i, dtype=torch.bfloat16).view(B, T, KV, hd)
+                    vc = ops.fill_normal(B * T * KV * hd, seed=11 + 2 * i, dtype=torch.bfloat16).view(B, T, KV, hd)
+                    kvs.append((kc, vc))
+                q = ops.fill_normal(B * H * hd, seed=3, dtype=torch.bfloat16).view(B, H, hd)
+                out = torch.empty_like(q)
+                nbytes = L.llama_attn_workspace_size(B, H, KV, hd, T)
+                ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda")
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+
+                def call(kc, vc):
+                    check(L.llama_attn_decode_bf16(s.cuda_stream, B, H, KV, hd, T, T, q.data_ptr(), kc.data_ptr(),
+                                                   vc.data_ptr(), out.data_ptr(), ws.data_ptr(), nbytes))
+                with torch.cuda.stream(s):
+                    call(*kvs[0])
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for kc, vc in kvs:
+                        call(kc, vc)
+                for _ in range(args.warmup):
+                    g.replay()
+                torch.cuda.synchronize()
+                st = torch.cuda.current_stream()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(args.steps):
+                    g.replay()
+                e1.record(st)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
+                byts = cache + 2 * B * H * hd * 2
+                rows.append({"heads": f"{H}q/{KV}kv", "hd": hd, "batch": B, "ctx": T, "us": round(us, 2),
+                             "gbs": round(byts / us / 1e3, 1), "frac": round(byts / us / 1e3 / peak, 3),
+                             "in_l2": copies * cache <= (100 << 20)})
+                del kvs, g
+                torch.cuda.empty_cache()
+    big = [r for r in rows if not r["in_l2"]]
+    line = {"metric": "flash-decode attention config2: HBM fraction (caches > L2)",
+            "value": max(r["frac"] for r in big) if big else None, "unit": "fraction of measured HBM GB/s",
+            "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "bf16 q/K/V/out, fp32 softmax", "data": "synthetic N(0,1) bf16",
+            "config": {"workload": "config2", "shapes": ["32q/4kv hd64", "32q/8kv hd128"], "ctx": ctxs,
+                       "batch": batches, "l2": "rotated caches > 300 MB where a cache is smaller"},
+            "hbm_peak_gbs": peak, "peak_kind": peak_kind, "table": rows}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def gemv_config0(torch, peak):
     """Config 0 GEMV (fp4_gemv through the C ABI) over 64 rotated weight copies,
     captured in one CUDA graph (no host launch gaps), CUDA-event timed."""
@@ -327,6 +398,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config3", action="store_true", help="fp4_mma sweep of BASELINE config 3 instead of decode")
     ap.add_argument("--c3-m", default="16,64,256,512")
+    ap.add_argument("--config2", action="store_true", help="attention sweep of BASELINE config 2 instead of decode")
+    ap.add_argument("--c2-ctx", default="512,2048,8192,32768")
+    ap.add_argument("--c2-batch", default="1,8,64")
     ap.add_argument("--c3-linears", default=",".join(C3_LINEARS))
     args = ap.parse_args()
     assert args.warmup >= 3, "timing rules: at least 3 warm-up steps"
@@ -334,6 +408,8 @@ def main():
         return run_reference(args)
     if args.config3:
         return run_config3(args)
+    if args.config2:
+        return run_config2(args)
 
     import torch
     rank = int(os.environ.get("RANK", "0"))
