@@ -349,6 +349,68 @@ def run_config2(args):
     return 0
 
 
+def run_config4(args):
+    """Llama-3-8B-shape MXFP4 decoder, tensor-parallel over the
+    torchrun ranks (1 process per GPU; in-graph NVLink peer-memory allreduce after O
+    and down, cross-rank argmax), batch 1, greedy decode at a 4096-token context.
+    The context is 4096 positions of zero-filled KV cache (attention reads all of
+    them; the prompt's values do not change the work), so no 4096-token prefill is
+    timed.  Step = one decode token of the whole TP group; value = tokens / max
+    over ranks of the device time."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from fp4x import engine, tp
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    ctx = args.c4_ctx
+    cfg = dict(engine.LLAMA3_8B, max_seq=ctx + args.warmup + args.steps + 8)
+    m = tp.create_model(cfg) if world > 1 else engine.Model(cfg)
+    path = m.path
+    m.forward(1, ctx - 1, want_logits=False)  # device state: position ctx - 1 done
+    m.decode_steps(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(st)
+        m.decode_steps(args.steps)
+        e1.record(st)
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) * 1e-3
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    wbytes = m.weight_bytes()  # this rank's shard
+    m.close()
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        per_tok = t / args.steps
+        line = {"metric": "config4 Llama-3-8B-shape MXFP4 decode tok/s (batch 1, TP)", "value": args.steps / t,
+                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": per_tok * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": DTYPES.get(path, path), "data": "synthetic (seeded N(0,0.02) weights -> MXFP4)",
+                "config": {"workload": "config4", "batch": 1, "context": ctx, "tp": world, "path": path,
+                           "kv": "zero-filled cache of ctx positions (prefill not timed)"},
+                "roofline": {"bound": "hbm", "kernel": f"decode token ({path} path), rank 0 shard",
+                             "achieved": wbytes / per_tok / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": wbytes / per_tok / 1e9 / peak, "bytes_per_launch": wbytes,
+                             "peak_kind": peak_kind},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def gemv_config0(torch, peak):
     """Config 0 GEMV (fp4_gemv through the C ABI) over 64 rotated weight copies,
     captured in one CUDA graph (no host launch gaps), CUDA-event timed."""
@@ -399,6 +461,8 @@ def main():
     ap.add_argument("--config3", action="store_true", help="fp4_mma sweep of BASELINE config 3 instead of decode")
     ap.add_argument("--c3-m", default="16,64,256,512")
     ap.add_argument("--config2", action="store_true", help="attention sweep of BASELINE config 2 instead of decode")
+    ap.add_argument("--config4", action="store_true", help="Llama-3-8B-shape TP decode (torchrun ranks) instead")
+    ap.add_argument("--c4-ctx", type=int, default=4096)
     ap.add_argument("--c2-ctx", default="512,2048,8192,32768")
     ap.add_argument("--c2-batch", default="1,8,64")
     ap.add_argument("--c3-linears", default=",".join(C3_LINEARS))
@@ -410,6 +474,8 @@ def main():
         return run_config3(args)
     if args.config2:
         return run_config2(args)
+    if args.config4:
+        return run_config4(args)
 
     import torch
     rank = int(os.environ.get("RANK", "0"))

@@ -232,6 +232,21 @@ FP4X_API int llama_decode_steps(fp4x_llama_model *m, fp4x_stream_t stream, uint3
  * with CUDA-core MXFP4 decode, 0 = CUDA graph of fused per-layer kernels.
  * FP4X_DECODE_PATH=graph|persistent selects 0|1 at creation. */
 FP4X_API int llama_model_set_path(fp4x_llama_model *m, int path);
+/* Tensor parallelism (no counterpart in the single-GPU
+ * reference): create the model on every rank with cfg.tp_rank / cfg.tp_size set
+ * (one process per GPU; KV heads and ffn/32 must split evenly).  Each rank holds
+ * its shard: the q/k/v rows of its heads, the O columns of those heads, its
+ * gate/up rows and down columns, and vocab rows [v0, v0 + vocab_local) of
+ * lm_head.  Then exchange the 64-byte handles (llama_model_tp_handle on every
+ * rank, gathered in rank order by the host) and call llama_model_tp_connect on
+ * every rank; it maps the peers' exchange areas (CUDA IPC over NVLink) and builds
+ * the decode graph, whose O and down projections end in an in-graph peer-memory
+ * allreduce and whose lm_head ends in a cross-rank argmax.  All ranks must then
+ * issue the same calls (llama_forward / llama_generate / decode steps) in the
+ * same order.  llama_forward returns this rank's logits slice. */
+FP4X_API int llama_model_tp_handle(fp4x_llama_model *m, void *handle_out /* 64 bytes */);
+FP4X_API int llama_model_tp_connect(fp4x_llama_model *m, const void *handles /* tp_size x 64 bytes */);
+FP4X_API int llama_model_shard(const fp4x_llama_model *m, uint32_t *v0, uint32_t *vocab_local);
 FP4X_API int llama_model_get_path(const fp4x_llama_model *m);
 /* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-587, EOS
  * ignored): prefill the prompt one position at a time, then n_gen tokens.

@@ -31,7 +31,8 @@
 namespace fp4x {
 namespace quant {
 int init_mxfp4_rowmap(cudaStream_t stream, uint64_t seed, float sigma, uint32_t n, uint32_t k, uint8_t *packed,
-                      uint8_t *scales, int mode, uint32_t off, uint32_t hd);
+                      uint8_t *scales, int mode, uint32_t off, uint32_t hd, uint32_t row0 = 0, uint32_t k_global = 0,
+                      uint32_t col0 = 0);
 }
 }  // namespace fp4x
 
@@ -53,7 +54,11 @@ struct LayerW {
 };
 
 struct fp4x_llama_model {
-    fp4x_llama_config cfg;
+    fp4x_llama_config cfg;  // the whole model
+    fp4x_llama_config lc;   // this rank's shard: n_heads, n_kv_heads, ffn, vocab per rank (== cfg without TP)
+    uint32_t v0 = 0;        // first vocab row of this rank's lm_head shard
+    float *part = nullptr;  // row-parallel partial outputs [dim] (tensor parallel)
+    fp4x::tp::Exchange *xc = nullptr;
     int device = 0;
     std::vector<void *> allocs;
     std::vector<LayerW> layers;
@@ -183,13 +188,19 @@ int validate_config(const fp4x_llama_config &c) {
     FP4X_REQUIRE(c.dim % 32 == 0 && c.ffn % 32 == 0, "llama config: dim and ffn must be multiples of 32");
     FP4X_REQUIRE(c.dim <= gemv::kMaxK && c.ffn <= gemv::kMaxK && c.n_heads * c.head_dim <= gemv::kMaxK,
                  "llama config: contraction length above %u", gemv::kMaxK);
-    FP4X_REQUIRE(c.tp_size <= 1, "llama config: tensor parallelism goes through llama_model_create_tp");
+    if (c.tp_size > 1) {
+        const uint32_t T = c.tp_size;
+        FP4X_REQUIRE(c.tp_rank < T && T <= 8, "llama config: tp_rank %u of tp_size %u (at most 8)", c.tp_rank, T);
+        FP4X_REQUIRE(c.n_kv_heads % T == 0, "llama config: %u KV heads do not split over %u ranks", c.n_kv_heads, T);
+        FP4X_REQUIRE(c.ffn % (32 * T) == 0, "llama config: ffn %u does not split over %u ranks in 32-blocks", c.ffn, T);
+    }
     return FP4X_OK;
 }
 
 // One token of the model on `st` (captured into the graph).
 int enqueue_token(fp4x_llama_model *m, cudaStream_t st) {
-    const fp4x_llama_config &c = m->cfg;
+    const fp4x_llama_config &c = m->lc;
+    const bool tp = m->xc != nullptr;
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     const bool pdl = m->pdl;
     uint32_t *tok = m->state, *pos = m->state + 1;
@@ -216,8 +227,9 @@ int enqueue_token(fp4x_llama_model *m, cudaStream_t st) {
         }
         // 3. O + residual
         a = gemv::Args{};
-        a.n = c.dim, a.k = qd, a.w = L.o.w, a.scales = L.o.s, a.x = m->att, a.y = m->x;
-        FP4X_TRY(gemv::launch_fused(st, gemv::PRO_NONE, gemv::EPI_RESIDUAL, a, pdl));
+        a.n = c.dim, a.k = qd, a.w = L.o.w, a.scales = L.o.s, a.x = m->att, a.y = tp ? m->part : m->x;
+        FP4X_TRY(gemv::launch_fused(st, gemv::PRO_NONE, tp ? gemv::EPI_STORE : gemv::EPI_RESIDUAL, a, pdl));
+        if (tp) FP4X_TRY(tp::allreduce_add(st, m->xc, m->part, m->x, pdl));  // row-parallel O
         // 4. RMSNorm + gate/up + SwiGLU
         a = gemv::Args{};
         a.n = 2 * c.ffn, a.k = c.dim, a.w = L.gu.w, a.scales = L.gu.s, a.x = m->x, a.y = m->s;
@@ -225,13 +237,15 @@ int enqueue_token(fp4x_llama_model *m, cudaStream_t st) {
         FP4X_TRY(gemv::launch_fused(st, gemv::PRO_RMSNORM, gemv::EPI_SWIGLU, a, pdl));
         // 5. down + residual
         a = gemv::Args{};
-        a.n = c.dim, a.k = c.ffn, a.w = L.down.w, a.scales = L.down.s, a.x = m->s, a.y = m->x;
-        FP4X_TRY(gemv::launch_fused(st, gemv::PRO_NONE, gemv::EPI_RESIDUAL, a, pdl));
+        a.n = c.dim, a.k = c.ffn, a.w = L.down.w, a.scales = L.down.s, a.x = m->s, a.y = tp ? m->part : m->x;
+        FP4X_TRY(gemv::launch_fused(st, gemv::PRO_NONE, tp ? gemv::EPI_STORE : gemv::EPI_RESIDUAL, a, pdl));
+        if (tp) FP4X_TRY(tp::allreduce_add(st, m->xc, m->part, m->x, pdl));  // row-parallel down
     }
     gemv::Args a = {};
     a.n = c.vocab, a.k = c.dim, a.w = m->lm_head.w, a.scales = m->lm_head.s, a.x = m->x, a.y = m->logits;
     a.norm_w = m->final_norm, a.eps = c.eps;
     FP4X_TRY(gemv::launch_fused(st, gemv::PRO_RMSNORM, gemv::EPI_STORE, a, pdl));
+    if (tp) return tp::argmax_advance(st, m->xc, c.vocab, m->v0, m->logits, m->state, m->prompt, m->out, pdl);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -264,28 +278,38 @@ int build_graph(fp4x_llama_model *m) {
 }
 
 int init_weights(fp4x_llama_model *m, cudaStream_t st) {
-    const fp4x_llama_config &c = m->cfg;
-    const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+    // shard of rank r (the whole model without TP): q rows of heads [r*H_l, ...), k/v
+    // rows of KV heads [r*KV_l, ...), O columns of those q heads, gate/up rows and
+    // down columns [r*ffn_l, ...), lm_head rows [v0, v0 + vocab_l)
+    const fp4x_llama_config &c = m->lc, &g = m->cfg;
+    const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd, r = g.tp_size > 1 ? g.tp_rank : 0;
+    const uint32_t gqd = g.n_heads * hd;
     auto tseed = [&](uint32_t id) { return hash64(c.seed, id); };
     const float sig = 0.02f;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
         LayerW &L = m->layers[l];
         const uint32_t base = T_LAYER0 + 8 * l;
         // QKV: q and k rope-paired, v natural, concatenated
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_Q), sig, qd, c.dim, L.qkv.w, L.qkv.s, 1, 0, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_K), sig, kvd, c.dim, L.qkv.w, L.qkv.s, 1, qd, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_V), sig, kvd, c.dim, L.qkv.w, L.qkv.s, 0, qd + kvd, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_O), sig, c.dim, qd, L.o.w, L.o.s, 0, 0, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_GATE), sig, c.ffn, c.dim, L.gu.w, L.gu.s, 2, 0, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_UP), sig, c.ffn, c.dim, L.gu.w, L.gu.s, 2, 8, hd));
-        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_DOWN), sig, c.dim, c.ffn, L.down.w, L.down.s, 0, 0, hd));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_Q), sig, qd, c.dim, L.qkv.w, L.qkv.s, 1, 0, hd, r * qd));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_K), sig, kvd, c.dim, L.qkv.w, L.qkv.s, 1, qd, hd, r * kvd));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_V), sig, kvd, c.dim, L.qkv.w, L.qkv.s, 0, qd + kvd, hd,
+                                          r * kvd));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_O), sig, c.dim, qd, L.o.w, L.o.s, 0, 0, hd, 0, gqd,
+                                          r * qd));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_GATE), sig, c.ffn, c.dim, L.gu.w, L.gu.s, 2, 0, hd,
+                                          r * c.ffn));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_UP), sig, c.ffn, c.dim, L.gu.w, L.gu.s, 2, 8, hd,
+                                          r * c.ffn));
+        FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(base + M_DOWN), sig, c.dim, c.ffn, L.down.w, L.down.s, 0, 0, hd, 0,
+                                          g.ffn, r * c.ffn));
         fill_f32_kernel<<<8, 256, 0, st>>>(L.attn_norm, 1.0f, c.dim);
         fill_f32_kernel<<<8, 256, 0, st>>>(L.ffn_norm, 1.0f, c.dim);
         FP4X_CUDA(cudaMemsetAsync(L.kc, 0, (size_t)c.max_seq * kvd * 2, st));
         FP4X_CUDA(cudaMemsetAsync(L.vc, 0, (size_t)c.max_seq * kvd * 2, st));
     }
-    FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(T_LMHEAD), sig, c.vocab, c.dim, m->lm_head.w, m->lm_head.s, 0, 0, hd));
-    FP4X_TRY(fp4x_fill_normal_bf16((fp4x_stream_t)st, tseed(T_EMBED), 0, sig, m->embed, (size_t)c.vocab * c.dim));
+    FP4X_TRY(quant::init_mxfp4_rowmap(st, tseed(T_LMHEAD), sig, c.vocab, c.dim, m->lm_head.w, m->lm_head.s, 0, 0, hd,
+                                      m->v0));
+    FP4X_TRY(fp4x_fill_normal_bf16((fp4x_stream_t)st, tseed(T_EMBED), 0, sig, m->embed, (size_t)g.vocab * c.dim));
     fill_f32_kernel<<<8, 256, 0, st>>>(m->final_norm, 1.0f, c.dim);
     FP4X_TRY(llama_rope_tables((fp4x_stream_t)st, c.max_seq, hd, (double)c.rope_theta, m->cos_t, m->sin_t));
     return check_launch("init_weights");
@@ -297,8 +321,15 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
     fp4x_llama_model *m = new (std::nothrow) fp4x_llama_model();
     if (!m) return FP4X_ENOMEM;
     m->cfg = *cfg;
+    m->lc = *cfg;
+    if (cfg->tp_size > 1) {  // this rank's shard sizes
+        const uint32_t T = cfg->tp_size, per = (cfg->vocab + T * 16 - 1) / (T * 16) * 16;
+        m->lc.n_heads = cfg->n_heads / T, m->lc.n_kv_heads = cfg->n_kv_heads / T, m->lc.ffn = cfg->ffn / T;
+        m->v0 = std::min(cfg->vocab, cfg->tp_rank * per);
+        m->lc.vocab = std::min(cfg->vocab, m->v0 + per) - m->v0;
+    }
     cudaGetDevice(&m->device);
-    const fp4x_llama_config &c = m->cfg;
+    const fp4x_llama_config &c = m->lc;
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     int rc = FP4X_OK;
     auto fail = [&](int r) {
@@ -319,8 +350,10 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
         L.kc = m->kv + (size_t)l * c.max_seq * kvd;
         L.vc = m->kv + (size_t)(c.n_layers + l) * c.max_seq * kvd;
     }
-    if (!rc) rc = alloc_q(m, m->lm_head, c.vocab, c.dim);
-    if (!rc) rc = alloc(m, &m->embed, (size_t)c.vocab * c.dim);
+    if (!rc) rc = alloc_q(m, m->lm_head, std::max(1u, c.vocab), c.dim);
+    if (!rc) rc = alloc(m, &m->embed, (size_t)m->cfg.vocab * c.dim);
+    if (!rc) rc = alloc(m, &m->part, c.dim);
+    if (!rc && m->cfg.tp_size > 1) rc = tp::create(&m->xc, m->cfg.tp_rank, m->cfg.tp_size, c.dim);
     if (!rc) rc = alloc(m, &m->final_norm, c.dim);
     if (!rc) rc = alloc(m, &m->cos_t, (size_t)c.max_seq * hd / 2);
     if (!rc) rc = alloc(m, &m->sin_t, (size_t)c.max_seq * hd / 2);
@@ -344,6 +377,10 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
         if (cudaMemcpyAsync(m->state, st, sizeof(st), cudaMemcpyHostToDevice, m->cap_stream) != cudaSuccess ||
             cudaStreamSynchronize(m->cap_stream) != cudaSuccess)
             rc = cuda_fail("llama_model_create: init", cudaGetLastError());
+    }
+    if (!rc && m->xc) {  // tensor parallel: graph path only, built by llama_model_tp_connect
+        *out = m;
+        return FP4X_OK;
     }
     if (!rc) rc = build_graph(m);
     if (!rc) {
@@ -434,6 +471,7 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
     }
     persist::destroy(m->pe);
     ptc::destroy(m->pt);
+    tp::destroy(m->xc);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return FP4X_OK;
@@ -441,8 +479,8 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
 
 extern "C" int llama_model_reset(fp4x_llama_model *m, fp4x_stream_t stream) {
     FP4X_REQUIRE(m, "llama_model_reset: null model");
-    const uint32_t kvd = m->cfg.n_kv_heads * m->cfg.head_dim;
-    FP4X_CUDA(cudaMemsetAsync(m->kv, 0, (size_t)2 * m->cfg.n_layers * m->cfg.max_seq * kvd * 2,
+    const uint32_t kvd = m->lc.n_kv_heads * m->lc.head_dim;
+    FP4X_CUDA(cudaMemsetAsync(m->kv, 0, (size_t)2 * m->lc.n_layers * m->lc.max_seq * kvd * 2,
                               (cudaStream_t)stream));
     return FP4X_OK;
 }
@@ -483,7 +521,7 @@ extern "C" int llama_forward(fp4x_llama_model *m, fp4x_stream_t stream, uint32_t
     FP4X_TRY(run_tokens(m, st, 1));
     if (next_host) FP4X_CUDA(cudaMemcpyAsync(next_host, m->state + 2, 4, cudaMemcpyDeviceToHost, st));
     if (logits_host)
-        FP4X_CUDA(cudaMemcpyAsync(logits_host, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
+        FP4X_CUDA(cudaMemcpyAsync(logits_host, m->logits, (size_t)m->lc.vocab * 4, cudaMemcpyDeviceToHost, st));
     FP4X_CUDA(cudaStreamSynchronize(st));
     return FP4X_OK;
 }
@@ -526,7 +564,7 @@ extern "C" int llama_generate(fp4x_llama_model *m, fp4x_stream_t stream, const u
 extern "C" int llama_model_export_tensor(fp4x_llama_model *m, uint32_t tensor_id, uint8_t *packed_host,
                                          uint8_t *scales_host, uint32_t *n_out, uint32_t *k_out) {
     FP4X_REQUIRE(m, "llama_model_export_tensor: null model");
-    const fp4x_llama_config &c = m->cfg;
+    const fp4x_llama_config &c = m->lc;  // this rank's shard under tensor parallelism
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     const QMat *src = nullptr;
     uint32_t n = 0, k = 0, mode = 0, off = 0;
@@ -588,4 +626,28 @@ extern "C" size_t llama_model_weight_bytes(const fp4x_llama_model *m) {
         b += ((size_t)L.qkv.n * L.qkv.k + (size_t)L.o.n * L.o.k + (size_t)L.gu.n * L.gu.k +
               (size_t)L.down.n * L.down.k) * 17 / 32;
     return b;
+}
+
+// ---------------------------------------------------------------- tensor parallel
+
+extern "C" int llama_model_tp_handle(fp4x_llama_model *m, void *handle_out) {
+    FP4X_REQUIRE(m && handle_out, "llama_model_tp_handle: null pointer");
+    FP4X_REQUIRE(m->xc, "llama_model_tp_handle: the model was not created with tp_size > 1");
+    cudaSetDevice(m->device);
+    return tp::export_handle(m->xc, handle_out);
+}
+
+extern "C" int llama_model_tp_connect(fp4x_llama_model *m, const void *handles) {
+    FP4X_REQUIRE(m && handles, "llama_model_tp_connect: null pointer");
+    FP4X_REQUIRE(m->xc, "llama_model_tp_connect: the model was not created with tp_size > 1");
+    cudaSetDevice(m->device);
+    FP4X_TRY(tp::connect(m->xc, handles));
+    return build_graph(m);
+}
+
+extern "C" int llama_model_shard(const fp4x_llama_model *m, uint32_t *v0, uint32_t *vocab_local) {
+    FP4X_REQUIRE(m, "llama_model_shard: null model");
+    if (v0) *v0 = m->v0;
+    if (vocab_local) *vocab_local = m->lc.vocab;
+    return FP4X_OK;
 }

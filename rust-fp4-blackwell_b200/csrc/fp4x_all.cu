@@ -8,4 +8,5 @@
 #include "mma.cu"
 #include "persist.cu"
 #include "persist_tc.cu"
+#include "tp.cu"
 #include "engine.cu"

@@ -30,11 +30,11 @@ constexpr int kCons = kCW * 32;           // consumer threads
 constexpr int kThreads = kCons + 64;      // + MMA warp + producer warp
 constexpr int kMaxSlots = 16;                // chunks in flight (barrier pairs)
 constexpr int kMaxOps = 48;               // chunk ops of one layer
-constexpr int kMaxLmOps = 40;             // chunk ops of the lm_head
+constexpr int kMaxLmOps = 64;             // chunk ops of the lm_head
 constexpr int kMaxAUnits = 4;             // QKV (tile, k-range) units per CTA
 constexpr int kMaxPairs = 12;             // (head, O tile) pairs per CTA
 constexpr int kMaxHeads = 4;              // heads attended per CTA
-constexpr int kMaxLm = 4;                 // lm_head tiles per CTA
+constexpr int kMaxLm = 8;                 // lm_head tiles per CTA
 constexpr int kMaxBlkPerChunk = 8;
 constexpr uint32_t kSlotTarget = 34816;  // chunk bytes aimed at (one cp.async.bulk each)
 constexpr uint32_t kBlk64 = 4096, kBlk32 = 2048, kAtom = 512;

@@ -164,15 +164,20 @@ __device__ __forceinline__ uint32_t map_row(uint32_t r, int mode, uint32_t off, 
     return r + off;
 }
 
+// Rows [row0, row0 + n) and columns [col0, col0 + k) of the global [*][k_global]
+// tensor `seed` (a tensor-parallel shard; row0 = col0 = 0, k_global = k for the
+// whole tensor): element (R, C) draws normal(seed, R * k_global + C).
 __global__ void init_mxfp4_rowmap_kernel(uint64_t seed, float sigma, uint32_t n, uint32_t k, uint8_t *__restrict__ packed,
-                                         uint8_t *__restrict__ scales, int mode, uint32_t off, uint32_t hd) {
+                                         uint8_t *__restrict__ scales, int mode, uint32_t off, uint32_t hd,
+                                         uint32_t row0, uint32_t k_global, uint32_t col0) {
     const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t nbr = k / 32;
     if (blk >= (uint64_t)n * nbr) return;
     const uint32_t r = (uint32_t)(blk / nbr), b = (uint32_t)(blk % nbr);
+    const uint64_t e0 = (uint64_t)(row0 + r) * k_global + col0 + 32u * b;
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = normal_draw(seed, blk * 32 + i, sigma);
+    for (int i = 0; i < 32; ++i) v[i] = normal_draw(seed, e0 + i, sigma);
     uint4 p;
     uint8_t s;
     quant_block_mxfp4(v, p, s);
@@ -191,9 +196,11 @@ namespace quant {
 // Engine helper: generate tensor `seed` ([n][k], N(0, sigma)) straight into a
 // fused layout (row map above).
 int init_mxfp4_rowmap(cudaStream_t stream, uint64_t seed, float sigma, uint32_t n, uint32_t k, uint8_t *packed,
-                      uint8_t *scales, int mode, uint32_t off, uint32_t hd) {
+                      uint8_t *scales, int mode, uint32_t off, uint32_t hd, uint32_t row0, uint32_t k_global,
+                      uint32_t col0) {
     const uint64_t nb = (uint64_t)n * (k / 32);
-    init_mxfp4_rowmap_kernel<<<grid_for(nb, 128), 128, 0, stream>>>(seed, sigma, n, k, packed, scales, mode, off, hd);
+    init_mxfp4_rowmap_kernel<<<grid_for(nb, 128), 128, 0, stream>>>(seed, sigma, n, k, packed, scales, mode, off, hd,
+                                                                     row0, k_global ? k_global : k, col0);
     return check_launch("init_mxfp4_rowmap");
 }
 }  // namespace quant

@@ -1,0 +1,291 @@
+// tp.cu -- tensor parallelism for the decode graph: the
+// exchange area every rank shares over NVLink, the row-parallel allreduce that
+// follows the O and down projections (llama_run/src/main.rs:522-530 with the
+// contraction split across ranks), and the vocab-parallel argmax.
+//
+// One process per GPU.  Each rank cudaMallocs an exchange area and exports it with
+// CUDA IPC; after the host has passed every rank's handle to every rank
+// (llama_model_tp_connect), rank r maps the others' areas and its kernels write
+// straight into them with peer stores:
+//   area = slots[2][kMaxRanks][dim] f32 | flags[2][kMaxRanks] u32 |
+//          argv[2][kMaxRanks] f32 | argi[2][kMaxRanks] u32 | aflags[2][kMaxRanks] u32
+// Exchange number n (a per-rank device counter; every rank runs the same sequence)
+// uses phase n & 1 and epoch n / 2 + 1: rank r stores its vector into slot
+// [phase][r] of every area, fences at system scope, raises flag [phase][r] to the
+// epoch everywhere, waits (bounded) until all flags of its own area reach the epoch,
+// and sums the slots in rank order, so every rank gets the same bits.  Two phases
+// suffice: rank r reaches exchange n+2 only after every rank finished n+1, hence
+// after every rank finished reading the phase of n.  No multicast object and no
+// library collective is involved.
+#include "common.cuh"
+
+#include <cstring>
+
+namespace fp4x {
+namespace tp {
+
+constexpr uint32_t kMaxRanks = 8;
+constexpr uint32_t kThreads = 1024;
+
+struct Peers {
+    uint8_t *area[kMaxRanks];
+};
+
+struct Layout {
+    size_t slots, flags, argv, argi, aflags, total;
+};
+
+__host__ __device__ inline Layout layout(uint32_t dim) {
+    Layout L;
+    L.slots = 0;
+    L.flags = (size_t)2 * kMaxRanks * dim * 4;
+    L.argv = L.flags + 2 * kMaxRanks * 4;
+    L.argi = L.argv + 2 * kMaxRanks * 4;
+    L.aflags = L.argi + 2 * kMaxRanks * 4;
+    L.total = (L.aflags + 2 * kMaxRanks * 4 + 255) / 256 * 256;
+    return L;
+}
+
+struct Exchange {
+    uint32_t rank = 0, size = 1, dim = 0;
+    uint8_t *local = nullptr;  // this rank's area (exported)
+    Peers peers = {};          // every rank's area in this process (peers[rank] = local)
+    uint32_t *count = nullptr; // completed exchanges (device)
+    bool connected = false;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Threads [0, size) wait until flag[src] >= epoch (bounded); returns false on timeout.
+__device__ bool wait_flags(const uint32_t *flags, uint32_t size, uint32_t epoch) {
+    __shared__ uint32_t ok;
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < size) {
+        uint32_t i = 0;
+        while (ld_acquire_sys(flags + threadIdx.x) < epoch) {
+            if (++i > kSpinLimit) {
+                raise_device_error(DEVERR_FLAG_TIMEOUT);
+                ok = 0;
+                break;
+            }
+            __nanosleep(100);
+        }
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// x[i] += sum over ranks of part[i] (rank order), with the residual folded in.
+__global__ void __launch_bounds__(kThreads) allreduce_add_kernel(Peers peers, const float *__restrict__ part,
+                                                                 float *__restrict__ x, uint32_t dim,
+                                                                 uint32_t *count, uint32_t rank, uint32_t size) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const Layout L = layout(dim);
+    const uint32_t n = *count, phase = n & 1u, epoch = n / 2 + 1;
+    for (uint32_t i = threadIdx.x * 4; i < dim; i += kThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(part + i);
+        for (uint32_t p = 0; p < size; ++p)
+            *reinterpret_cast<float4 *>(peers.area[p] + L.slots + ((size_t)(phase * kMaxRanks + rank) * dim + i) * 4) =
+                v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (uint32_t p = 0; p < size; ++p)
+            st_release_sys(reinterpret_cast<uint32_t *>(peers.area[p] + L.flags) + phase * kMaxRanks + rank, epoch);
+    }
+    const uint8_t *mine = peers.area[rank];
+    const bool ok = wait_flags(reinterpret_cast<const uint32_t *>(mine + L.flags) + phase * kMaxRanks, size, epoch);
+    if (ok)
+        for (uint32_t i = threadIdx.x * 4; i < dim; i += kThreads * 4) {
+            float4 acc = *reinterpret_cast<const float4 *>(x + i);
+            for (uint32_t s = 0; s < size; ++s) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(
+                    mine + L.slots + ((size_t)(phase * kMaxRanks + s) * dim + i) * 4));
+                acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+            }
+            *reinterpret_cast<float4 *>(x + i) = acc;
+        }
+    __syncthreads();
+    if (threadIdx.x == 0) *count = n + 1;
+}
+
+__device__ __forceinline__ void argmax_merge(float &bv, uint32_t &bi, float ov, uint32_t oi) {
+    if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+    }
+}
+
+// Argmax over this rank's vocab slice [v0, v0 + n), exchange of (value, index)
+// with every rank, global argmax (larger value, ties to the lower index,
+// llama_run/src/main.rs:263-315), then the loop-state advance of
+// llama_run/src/main.rs:550-566 (every rank computes the same next token).
+__global__ void __launch_bounds__(kThreads) argmax_advance_kernel(Peers peers, uint32_t dim, uint32_t n, uint32_t v0,
+                                                                  const float *__restrict__ logits, uint32_t *count,
+                                                                  uint32_t rank, uint32_t size,
+                                                                  uint32_t *__restrict__ state,
+                                                                  const uint32_t *__restrict__ prompt,
+                                                                  uint32_t *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float mv[32];
+    __shared__ uint32_t mi[32];
+    const Layout L = layout(dim);
+    float bv = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) argmax_merge(bv, bi, logits[i], v0 + i);
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) mv[warp] = bv, mi[warp] = bi;
+    __syncthreads();
+    const uint32_t c = *count, phase = c & 1u, epoch = c / 2 + 1;
+    if (threadIdx.x == 0) {
+        float gv = -INFINITY;
+        uint32_t gi = 0xFFFFFFFFu;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) argmax_merge(gv, gi, mv[w], mi[w]);
+        for (uint32_t p = 0; p < size; ++p) {
+            reinterpret_cast<float *>(peers.area[p] + L.argv)[phase * kMaxRanks + rank] = gv;
+            reinterpret_cast<uint32_t *>(peers.area[p] + L.argi)[phase * kMaxRanks + rank] = gi;
+        }
+        __threadfence_system();
+        for (uint32_t p = 0; p < size; ++p)
+            st_release_sys(reinterpret_cast<uint32_t *>(peers.area[p] + L.aflags) + phase * kMaxRanks + rank, epoch);
+    }
+    const uint8_t *mine = peers.area[rank];
+    const bool ok = wait_flags(reinterpret_cast<const uint32_t *>(mine + L.aflags) + phase * kMaxRanks, size, epoch);
+    if (threadIdx.x == 0) {
+        float gv = -INFINITY;
+        uint32_t gi = 0;
+        if (ok)
+            for (uint32_t s = 0; s < size; ++s)
+                argmax_merge(gv, gi, __ldcg(reinterpret_cast<const float *>(mine + L.argv) + phase * kMaxRanks + s),
+                             __ldcg(reinterpret_cast<const uint32_t *>(mine + L.argi) + phase * kMaxRanks + s));
+        const uint32_t pos = state[1], n_prompt = state[3], cap = state[4];
+        state[2] = gi;
+        if (pos + 1 >= n_prompt && pos + 1 - n_prompt < cap) out[pos + 1 - n_prompt] = gi;
+        state[0] = (pos + 1 < n_prompt) ? prompt[pos + 1] : gi;
+        state[1] = pos + 1;
+        *count = c + 1;
+    }
+}
+
+// ---------------------------------------------------------------- host
+
+int create(Exchange **out, uint32_t rank, uint32_t size, uint32_t dim) {
+    FP4X_REQUIRE(size >= 2 && size <= kMaxRanks && rank < size, "tensor parallel: rank %u of %u (2..%u ranks)", rank,
+                 size, kMaxRanks);
+    FP4X_REQUIRE(dim % 4 == 0, "tensor parallel: dim %u %% 4 != 0", dim);
+    Exchange *x = new Exchange();
+    x->rank = rank, x->size = size, x->dim = dim;
+    const size_t bytes = layout(dim).total;
+    cudaError_t e = cudaMalloc(&x->local, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&x->count, 16);
+    if (e == cudaSuccess) e = cudaMemset(x->local, 0, bytes);
+    if (e == cudaSuccess) e = cudaMemset(x->count, 0, 16);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any peer can see the handle
+    if (e != cudaSuccess) {
+        if (x->local) cudaFree(x->local);
+        if (x->count) cudaFree(x->count);
+        delete x;
+        set_error("tensor parallel: exchange area: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    x->peers.area[rank] = x->local;
+    *out = x;
+    return FP4X_OK;
+}
+
+void destroy(Exchange *x) {
+    if (!x) return;
+    for (uint32_t p = 0; p < x->size; ++p)
+        if (p != x->rank && x->peers.area[p]) cudaIpcCloseMemHandle(x->peers.area[p]);
+    if (x->local) cudaFree(x->local);
+    if (x->count) cudaFree(x->count);
+    delete x;
+}
+
+int export_handle(Exchange *x, void *handle64) {
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, x->local);
+    if (e != cudaSuccess) {
+        set_error("tensor parallel: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle64, &h, sizeof(h));
+    return FP4X_OK;
+}
+
+int connect(Exchange *x, const void *handles) {
+    FP4X_REQUIRE(!x->connected, "tensor parallel: already connected");
+    for (uint32_t p = 0; p < x->size; ++p) {
+        if (p == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t *>(handles) + 64 * p, 64);
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            set_error("tensor parallel: cudaIpcOpenMemHandle(rank %u): %s", p, cudaGetErrorString(e));
+            return FP4X_ECUDA;
+        }
+        x->peers.area[p] = static_cast<uint8_t *>(ptr);
+    }
+    x->connected = true;
+    return FP4X_OK;
+}
+
+static int launch_cfg(cudaStream_t st, bool pdl, cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return FP4X_OK;
+}
+
+int allreduce_add(cudaStream_t st, Exchange *x, const float *part, float *y, bool pdl) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[1];
+    launch_cfg(st, pdl, cfg, attr);
+    const cudaError_t e =
+        cudaLaunchKernelEx(&cfg, allreduce_add_kernel, x->peers, part, y, x->dim, x->count, x->rank, x->size);
+    if (e != cudaSuccess) {
+        set_error("tensor parallel allreduce: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    return FP4X_OK;
+}
+
+int argmax_advance(cudaStream_t st, Exchange *x, uint32_t n, uint32_t v0, const float *logits, uint32_t *state,
+                   const uint32_t *prompt, uint32_t *out, bool pdl) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[1];
+    launch_cfg(st, pdl, cfg, attr);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_advance_kernel, x->peers, x->dim, n, v0, logits, x->count,
+                                             x->rank, x->size, state, prompt, out);
+    if (e != cudaSuccess) {
+        set_error("tensor parallel argmax: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    return FP4X_OK;
+}
+
+}  // namespace tp
+}  // namespace fp4x

@@ -44,6 +44,9 @@ SIGNATURES = {
     "llama_decode_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
     "llama_model_set_path": (C.c_int, [C.c_void_p, C.c_int]),
     "llama_model_get_path": (C.c_int, [C.c_void_p]),
+    "llama_model_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "llama_model_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "llama_model_shard": (C.c_int, [C.c_void_p, _u32p, _u32p]),
 }
 
 
@@ -101,9 +104,27 @@ class Model:
     def reset(self):
         check(self.L.llama_model_reset(self._h, self._st()))
 
+    def shard(self):
+        """(v0, vocab_local): the lm_head rows this rank holds (the whole vocab without TP)."""
+        v0, nv = C.c_uint32(0), C.c_uint32(0)
+        check(self.L.llama_model_shard(self._h, C.byref(v0), C.byref(nv)))
+        return v0.value, nv.value
+
+    def tp_handle(self) -> bytes:
+        """64-byte IPC handle of this rank's exchange area (tensor parallel)."""
+        buf = C.create_string_buffer(64)
+        check(self.L.llama_model_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Map every rank's exchange area (handles in rank order) and build the graph."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        check(self.L.llama_model_tp_connect(self._h, blob))
+
     def forward(self, token: int, pos: int, want_logits: bool = True):
+        """Next token and logits (this rank's vocab slice under tensor parallelism)."""
         nxt = np.zeros(1, np.uint32)
-        logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        logits = np.empty(self.shard()[1], np.float32) if want_logits else None
         check(self.L.llama_forward(self._h, self._st(), token, pos, _p(nxt, C.c_uint32),
                                    _p(logits, C.c_float) if want_logits else None))
         return int(nxt[0]), logits
