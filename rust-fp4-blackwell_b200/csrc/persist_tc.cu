@@ -75,7 +75,7 @@ __device__ __forceinline__ void mstamp(uint32_t) {}
     } while (0)
 
 struct Smem {
-    uint32_t bars, flag, red, sched, xv, bx, sfbx, bo, sfbo, bh, sfbh, qs, wst, gu, ring, total;
+    uint32_t bars, flag, red, sched, xv, bx, sfbx, bo, sfbo, bh, sfbh, qs, wst, gu, ps, ring, total;
 };
 
 __host__ __device__ inline uint32_t attn_k(const Params &p) { return kMaxHeads * p.hd; }
@@ -100,9 +100,10 @@ __host__ __device__ inline Smem smem_layout(const Params &p) {
     L.sfbo = take((attn_k(p) / 128 + 1 + 3) * 128, 128);
     L.bh = take(5 * 128, 128);                       // U <= 128: 4 k32 columns, then a zero column
     L.sfbh = take((2 + 3) * 128, 128);
-    L.qs = take(kMaxHeads * p.hd * 4, 16);
+    L.qs = take(kMaxGroup * p.hd * 4, 16);
     L.wst = take(kCW * (p.hd + 2) * 4, 16);
     L.gu = take(256 * 4, 16);
+    L.ps = take(kCW * kMaxGroup * 32 * 4, 16);  // split attention: per-warp probabilities
     L.ring = take(p.ring_bytes, 1024);
     L.total = off + 4096;  // MMA windows of partial tiles read up to 2 KB past a chunk
     return L;
@@ -597,30 +598,21 @@ __device__ void attend(Ctx &c, uint32_t l, uint32_t pos) {
     csync();
 }
 
-// B: fold the FFN delta into X (a slice per CTA), attention of this CTA's heads,
-// O-projection pairs (head, O tile) added into X.
-__device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_count) {
+// Fold the previous layer's FFN delta into X (a slice per CTA) and clear it.
+__device__ void fold_delta(Ctx &c, uint32_t l) {
+    const Params &p = *c.p;
+    const uint32_t per = (p.dim + gridDim.x - 1) / gridDim.x;
+    const uint32_t e0 = blockIdx.x * per, e1 = min(p.dim, e0 + per);
+    for (uint32_t e = e0 + threadIdx.x; e < e1; e += kCons) {
+        if (l > 0) red_add(&p.X[e], __ldcg(&p.Y[e]));
+        p.Y[e] = 0.0f;
+    }
+}
+
+// O projection of the attention output staged in xv ([head slot][hd] f32).
+__device__ void o_projection(Ctx &c, uint32_t lay_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
-    {
-        const uint32_t per = (p.dim + gridDim.x - 1) / gridDim.x;
-        const uint32_t e0 = blockIdx.x * per, e1 = min(p.dim, e0 + per);
-        for (uint32_t e = e0 + threadIdx.x; e < e1; e += kCons) {
-            if (l > 0) red_add(&p.X[e], __ldcg(&p.Y[e]));
-            p.Y[e] = 0.0f;
-        }
-    }
-    if (S.n_pairs == 0) return;
-    if (p.hd == 64) {
-        stage_qkv<64>(c, l, pos);
-        CST(6);
-        attend<64>(c, l, pos);
-    } else {
-        stage_qkv<128>(c, l, pos);
-        CST(6);
-        attend<128>(c, l, pos);
-    }
-    CST(7);
     decompose8(reinterpret_cast<const float *>(c.smem + c.L.xv), S.nh * p.hd, c.smem + c.L.bo, c.smem + c.L.sfbo,
                false);
     signal_operand(c, PH_O);
@@ -634,6 +626,218 @@ __device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_coun
         red_add(&p.X[S.pair_tile[i] * 128 + 32 * (warp & 3) + lane], s);
     }
     CST(10);
+}
+
+// B (short contexts): fold the FFN delta, attention of this CTA's heads over the
+// whole sequence, O-projection pairs (head, O tile) added into X.
+__device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_count) {
+    const Params &p = *c.p;
+    const Sched &S = *c.S;
+    fold_delta(c, l);
+    if (S.n_pairs == 0) return;
+    if (p.hd == 64) {
+        stage_qkv<64>(c, l, pos);
+        CST(6);
+        attend<64>(c, l, pos);
+    } else {
+        stage_qkv<128>(c, l, pos);
+        CST(6);
+        attend<128>(c, l, pos);
+    }
+    CST(7);
+    o_projection(c, lay_count);
+}
+
+// Split attention for long contexts, part 1: unit u = (KV head g, slice s) of the
+// sequence (one unit per CTA, units = n_kv * attn_slices), all q heads of the GQA
+// group at once (each K/V row read once per unit).  Lane = token for Q.K, lane =
+// head-dim pair for P.V (probabilities through shared memory).  The unit holding
+// the current position also RoPEs and appends its K/V (bf16).  Writes per head the
+// slice's (max, sum, unnormalised output) to attn_part[head][slice].
+template <int HD, int GRP>
+__device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
+    const Params &p = *c.p;
+    constexpr int NV = HD / 32;
+    constexpr uint32_t half = HD / 2;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+    const uint32_t slices = p.attn_slices, u = blockIdx.x;
+    if (u >= p.n_kv * slices) return;
+    const uint32_t g = u / slices, sl = u % slices, seq = pos + 1;
+    const uint32_t len = (seq + slices - 1) / slices, t_begin = min(seq, sl * len), t_end = min(seq, t_begin + len);
+    const uint32_t h0 = g * GRP;
+    float *qs = reinterpret_cast<float *>(c.smem + c.L.qs);  // [GRP][HD]
+    const float *cs = p.cos_t + (size_t)pos * half, *sn = p.sin_t + (size_t)pos * half;
+    const float scale = 1.0f / sqrtf((float)HD);
+    for (uint32_t i = tid; i < GRP * half; i += kCons) {
+        const uint32_t hh = i / half, j = i % half;
+        const float *qr = p.qkv + (h0 + hh) * HD;
+        const float q0 = __ldcg(qr + j), q1 = __ldcg(qr + j + half);
+        qs[hh * HD + j] = __fsub_rn(__fmul_rn(q0, cs[j]), __fmul_rn(q1, sn[j])) * scale;
+        qs[hh * HD + j + half] = __fadd_rn(__fmul_rn(q1, cs[j]), __fmul_rn(q0, sn[j])) * scale;
+    }
+    const size_t row = p.kvd;
+    uint16_t *kb = p.kc + (size_t)l * p.max_seq * row + g * HD, *vb = p.vc + (size_t)l * p.max_seq * row + g * HD;
+    if (t_end == seq && t_begin < seq && tid < half) {  // this unit holds the current position: append its K/V
+        const float *kr = p.qkv + p.qd + g * HD, *vr = p.qkv + p.qd + p.kvd + g * HD;
+        const uint32_t j = tid;
+        const float k0 = __ldcg(kr + j), k1 = __ldcg(kr + j + half);
+        kb[(size_t)pos * row + j] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(k0, cs[j]), __fmul_rn(k1, sn[j])));
+        kb[(size_t)pos * row + j + half] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(k1, cs[j]), __fmul_rn(k0, sn[j])));
+        vb[(size_t)pos * row + j] = f32_to_bf16_bits(__ldcg(vr + j));
+        vb[(size_t)pos * row + j + half] = f32_to_bf16_bits(__ldcg(vr + j + half));
+    }
+    csync();
+    float *ps = reinterpret_cast<float *>(c.smem + c.L.ps) + warp * (kMaxGroup * 32);
+    float m[GRP], lsum[GRP], o[GRP][NV];
+#pragma unroll
+    for (int h = 0; h < GRP; ++h) {
+        m[h] = -INFINITY, lsum[h] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) o[h][i] = 0.0f;
+    }
+    for (uint32_t t0 = t_begin + 32 * warp; t0 < t_end; t0 += 32 * kCW) {
+        const uint32_t t = t0 + lane;
+        const bool live = t < t_end;
+        float sc[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) sc[h] = 0.0f;
+        if (live) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)t * row);
+#pragma unroll
+            for (int cc = 0; cc < HD / 8; ++cc) {
+                const uint4 kq = __ldcg(kr + cc);
+                const uint32_t wv[4] = {kq.x, kq.y, kq.z, kq.w};
+                float kv[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    kv[2 * j] = __uint_as_float(wv[j] << 16);
+                    kv[2 * j + 1] = __uint_as_float(wv[j] & 0xFFFF0000u);
+                }
+#pragma unroll
+                for (int h = 0; h < GRP; ++h) {
+                    const float *q = qs + h * HD + 8 * cc;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) sc[h] += q[j] * kv[j];
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            const float sh = live ? sc[h] : -INFINITY;
+            const float mn = fmaxf(m[h], warp_max(sh));
+            const float alpha = __expf(m[h] - mn);
+            const float pr = live ? __expf(sh - mn) : 0.0f;
+            lsum[h] = lsum[h] * alpha + warp_sum(pr);
+            m[h] = mn;
+            ps[h * 32 + lane] = pr;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) o[h][i] *= alpha;
+        }
+        __syncwarp();
+        const uint32_t nt = min(32u, t_end - t0);
+#pragma unroll 4
+        for (uint32_t j = 0; j < nt; ++j) {
+            const uint32_t *vr = reinterpret_cast<const uint32_t *>(vb + (size_t)(t0 + j) * row);
+            float v[NV];
+#pragma unroll
+            for (int cc = 0; cc < HD / 64; ++cc) {
+                const uint32_t w = __ldcg(vr + 32 * cc + lane);
+                v[2 * cc] = __uint_as_float(w << 16);
+                v[2 * cc + 1] = __uint_as_float(w & 0xFFFF0000u);
+            }
+#pragma unroll
+            for (int h = 0; h < GRP; ++h) {
+                const float pr = ps[h * 32 + j];
+#pragma unroll
+                for (int i = 0; i < NV; ++i) o[h][i] += pr * v[i];
+            }
+        }
+        __syncwarp();
+    }
+    // merge the warps per head (fixed order), one head at a time through wst
+    float *wst = reinterpret_cast<float *>(c.smem + c.L.wst);  // [kCW][HD + 2]
+#pragma unroll 1
+    for (int h = 0; h < GRP; ++h) {
+        float *ws = wst + warp * (HD + 2);
+        float mh = m[0], lh = lsum[0];
+        float oh[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) oh[i] = o[0][i];
+#pragma unroll
+        for (int q = 1; q < GRP; ++q)
+            if (q == h) {
+                mh = m[q], lh = lsum[q];
+#pragma unroll
+                for (int i = 0; i < NV; ++i) oh[i] = o[q][i];
+            }
+        if (lane == 0) ws[0] = mh, ws[1] = lh;
+#pragma unroll
+        for (int cc = 0; cc < HD / 64; ++cc) {
+            ws[2 + 64 * cc + 2 * lane] = oh[2 * cc];
+            ws[2 + 64 * cc + 2 * lane + 1] = oh[2 * cc + 1];
+        }
+        csync();
+        float *rec = p.attn_part + ((size_t)(h0 + h) * slices + sl) * (HD + 2);
+        for (uint32_t d = tid; d < HD + 2; d += kCons) {
+            float M = -INFINITY;
+            for (int w = 0; w < kCW; ++w) M = fmaxf(M, wst[w * (HD + 2)]);
+            float v = M;
+            if (d > 0) {
+                v = 0.0f;
+                for (int w = 0; w < kCW; ++w) {
+                    const float mw = wst[w * (HD + 2)];
+                    v += (mw == -INFINITY) ? 0.0f : wst[w * (HD + 2) + d] * __expf(mw - M);
+                }
+            }
+            rec[d] = v;
+        }
+        csync();
+    }
+}
+
+// Split attention, part 1 (every CTA): fold the FFN delta, then this CTA's unit.
+__device__ void phase_attn_units(Ctx &c, uint32_t l, uint32_t pos) {
+    const Params &p = *c.p;
+    fold_delta(c, l);
+    const uint32_t group = p.n_heads / p.n_kv;
+    if (p.hd == 64) {
+        if (group == 8) attend_unit<64, 8>(c, l, pos);
+        else if (group == 4) attend_unit<64, 4>(c, l, pos);
+        else attend_unit<64, 2>(c, l, pos);
+    } else {
+        if (group == 8) attend_unit<128, 8>(c, l, pos);
+        else if (group == 4) attend_unit<128, 4>(c, l, pos);
+        else attend_unit<128, 2>(c, l, pos);
+    }
+    CST(6);
+}
+
+// Split attention, part 2 (after a grid barrier): combine the slices of this CTA's
+// heads into xv, then the O projection.
+__device__ void phase_attn_combine_o(Ctx &c, uint32_t lay_count) {
+    const Params &p = *c.p;
+    const Sched &S = *c.S;
+    if (S.n_pairs == 0) return;
+    const uint32_t hd = p.hd, slices = p.attn_slices;
+    float *xv = reinterpret_cast<float *>(c.smem + c.L.xv);
+    for (uint32_t i = threadIdx.x; i < S.nh * hd; i += kCons) {
+        const uint32_t hs = i / hd, d = i % hd;
+        const float *rec = p.attn_part + (size_t)(S.h0 + hs) * slices * (hd + 2);
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < slices; ++s) M = fmaxf(M, __ldcg(rec + s * (hd + 2)));
+        float L = 0.0f, O = 0.0f;
+        for (uint32_t s = 0; s < slices; ++s) {
+            const float ms = __ldcg(rec + s * (hd + 2));
+            if (ms == -INFINITY) continue;
+            const float f = __expf(ms - M);
+            L += __ldcg(rec + s * (hd + 2) + 1) * f;
+            O += __ldcg(rec + s * (hd + 2) + 2 + d) * f;
+        }
+        xv[i] = O / L;
+    }
+    csync();
+    CST(7);
+    o_projection(c, lay_count);
 }
 
 // C: zero a slice of the QKV sums (read in B, next written in the next layer's
@@ -964,7 +1168,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
                 phase_qkv(c, l, tok, lc);
                 if (!grid_barrier(c)) break;
                 CST(5);
-                phase_attn_o(c, l, pos, lc);
+                if (p.attn_slices && pos + 1 > kSplitMinSeq) {  // same decision in every CTA
+                    phase_attn_units(c, l, pos);
+                    if (!grid_barrier(c)) break;
+                    phase_attn_combine_o(c, lc);
+                } else {
+                    phase_attn_o(c, l, pos, lc);
+                }
                 if (!grid_barrier(c)) break;
                 CST(11);
                 phase_ffn(c, l, lc);
@@ -1335,6 +1545,10 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
     if (!rc) rc = dalloc(e, &X, c.dim);
     if (!rc) rc = dalloc(e, &Y, c.dim);
     if (!rc) rc = dalloc(e, &qkv, rows_qkv);
+    const uint32_t group = c.n_heads / c.n_kv_heads;
+    const uint32_t slices = (group == 2 || group == 4 || group == 8) ? (uint32_t)G / c.n_kv_heads : 0u;
+    float *apart = nullptr;
+    if (!rc && slices) rc = dalloc(e, &apart, (size_t)c.n_heads * slices * (hd + 2));
     if (!rc) rc = dalloc(e, &cval, (size_t)G);
     if (!rc) rc = dalloc(e, &cidx, (size_t)G);
     if (!rc) rc = dalloc(e, &djobs, jobs.size());
@@ -1366,6 +1580,7 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
     P.attn_norm = in.attn_norm, P.ffn_norm = in.ffn_norm, P.final_norm = in.final_norm;
     P.embed = in.embed, P.cos_t = in.cos_t, P.sin_t = in.sin_t, P.kc = in.kc, P.vc = in.vc;
     P.X = X, P.Y = Y, P.qkv = qkv, P.logits = in.logits, P.cand_val = cval, P.cand_idx = cidx;
+    P.attn_part = apart, P.attn_slices = slices;
     P.state = in.state, P.prompt = in.prompt, P.out = in.out, P.bar = bar, P.n_tokens = 0;
     e->p = P;
     e->grid = G;

@@ -34,6 +34,8 @@ constexpr int kMaxLmOps = 64;             // chunk ops of the lm_head
 constexpr int kMaxAUnits = 4;             // QKV (tile, k-range) units per CTA
 constexpr int kMaxPairs = 12;             // (head, O tile) pairs per CTA
 constexpr int kMaxHeads = 4;              // heads attended per CTA
+constexpr int kMaxGroup = 8;              // q heads per KV head (split attention units)
+constexpr uint32_t kSplitMinSeq = 512;    // longer contexts: attention split over (KV head, slice) units
 constexpr int kMaxLm = 8;                 // lm_head tiles per CTA
 constexpr int kMaxBlkPerChunk = 8;
 constexpr uint32_t kSlotTarget = 34816;  // chunk bytes aimed at (one cp.async.bulk each)
@@ -81,6 +83,8 @@ struct Params {
     const float *cos_t, *sin_t;                      // [max_seq][hd/2]
     uint16_t *kc, *vc;                               // [n_layers][max_seq][kvd] bf16
     float *X, *Y, *qkv, *logits;                     // residual, FFN delta, QKV sums, logits
+    float *attn_part;                                // [n_heads][attn_slices][hd + 2] split-attention partials
+    uint32_t attn_slices;                            // sequence slices per KV head (0: no split attention)
     float *cand_val;
     uint32_t *cand_idx;
     uint32_t *state;  // [0] tok [1] pos [2] next [3] n_prompt [4] out capacity

@@ -35,16 +35,16 @@ def shape_of(cfg, tid):
             4: (cfg["ffn"], cfg["dim"]), 5: (cfg["ffn"], cfg["dim"]), 6: (cfg["dim"], cfg["ffn"])}[m]
 
 
-def compare_logits(got, ref):
-    """1e-2 relative (rms floor) and the same greedy token unless the reference's
+def compare_logits(got, ref, tol=LOGIT_TOL):
+    """`tol` relative (rms floor) and the same greedy token unless the reference's
     top-2 margin is inside the tolerance band."""
     err = rel_rms(got, ref).max()
-    assert err <= LOGIT_TOL, err
+    assert err <= tol, err
     a, b = int(np.argmax(got)), int(np.argmax(ref))
     if a != b:
         top2 = np.sort(ref)[-2:]
         margin = (top2[1] - top2[0]) / np.sqrt(np.mean(ref.astype(np.float64) ** 2))
-        assert margin < LOGIT_TOL, f"argmax {a} vs {b} with margin {margin:.3e}"
+        assert margin < tol, f"argmax {a} vs {b} with margin {margin:.3e}"
     return err
 
 
@@ -164,3 +164,53 @@ def test_engine_tinyllama_config1(path):
                 assert gn == seq[pos + 1]
     ref.close()
     print(f"config1: worst logits rel err {worst:.3e}")
+
+
+def test_engine_llama8b_shape_paths_agree():
+    """BASELINE config 4 shape at TP = 1 (32 layers, d 4096, ffn 14336, 32q/8kv hd 128,
+    vocab 128256): the tensor-core persistent path against the CUDA-graph path (whose
+    kernels are checked against the oracle on the smaller shapes) on the same device
+    state.  Two results each within 1e-2 of the oracle differ by up to 2e-2 (the bf16
+    KV cache rounds the two paths' K/V sums, equal to ~1e-7, to possibly different
+    bf16 neighbours, and 32 layers compound it), so the bound here is 2e-2."""
+    cfg = dict(engine.LLAMA3_8B, max_seq=64)
+    toks = oracle.uniform_ids(11, cfg["vocab"], 6)
+    with engine.Model(cfg) as m:
+        assert m.path == "tensor", m.path
+        outs = {}
+        for path in ("graph", "tensor"):
+            m.set_path(path)
+            m.reset()
+            outs[path] = [m.forward(int(t), pos) for pos, t in enumerate(toks)]
+        for (ng, lg), (nt, lt) in zip(outs["graph"], outs["tensor"]):
+            compare_logits(lt, lg, tol=2 * LOGIT_TOL)
+        ids_g, ids_t = None, None
+        prompt = oracle.uniform_ids(12, cfg["vocab"], 4)
+        m.set_path("graph")
+        m.reset()
+        ids_g, _, _ = m.generate(prompt, 8)
+        m.set_path("tensor")
+        m.reset()
+        ids_t, _, _ = m.generate(prompt, 8)
+        assert np.mean(ids_t == ids_g) >= 0.75, (ids_t, ids_g)  # near-ties may flip a token
+
+
+@pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
+def test_engine_long_context_split_attention(cfg):
+    """Contexts above 512 positions switch the tensor path's attention to (KV head,
+    sequence slice) units with a cross-slice combine; logits must stay within 1e-2
+    of the oracle through the switch (teacher forcing on a seeded token stream)."""
+    cfg = dict(cfg, max_seq=700)
+    toks = oracle.uniform_ids(21, cfg["vocab"], 660)
+    ref = oracle.Model(cfg)
+    with engine.Model(cfg) as m:
+        assert m.path == "tensor"
+        worst = 0.0
+        for pos, t in enumerate(toks):
+            want = pos in (0, 100, 505, 511, 512, 513, 600, 659)
+            gn, gl = m.forward(int(t), pos, want_logits=want)
+            rn, rl = ref.forward(int(t), pos)
+            if want:
+                worst = max(worst, compare_logits(gl, rl))
+    ref.close()
+    print(f"long context: worst logits rel err {worst:.3e}")
