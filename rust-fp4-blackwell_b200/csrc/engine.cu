@@ -315,6 +315,56 @@ int init_weights(fp4x_llama_model *m, cudaStream_t st) {
     return check_launch("init_weights");
 }
 
+// The persistent decode kernels over this model's (shard's) weights; a path the
+// shape does not fit is left out with its reason.  Under tensor parallelism only
+// the tensor-core kernel is built, with its shared buffers in the exchange areas.
+int build_persistent(fp4x_llama_model *m, const ptc::TpIn *tpin) {
+    const fp4x_llama_config &c = m->lc;
+    const uint32_t kvd = c.n_kv_heads * c.head_dim;
+    int rc = FP4X_OK;
+    persist::BuildIn in;
+    in.cfg = c;
+    for (auto &L : m->layers) {
+        in.qkv.push_back({L.qkv.w, L.qkv.s, L.qkv.n, L.qkv.k});
+        in.o.push_back({L.o.w, L.o.s, L.o.n, L.o.k});
+        in.gu.push_back({L.gu.w, L.gu.s, L.gu.n, L.gu.k});
+        in.down.push_back({L.down.w, L.down.s, L.down.n, L.down.k});
+    }
+    in.lm = {m->lm_head.w, m->lm_head.s, m->lm_head.n, m->lm_head.k};
+    in.attn_norm = m->norms, in.ffn_norm = m->norms + (size_t)c.n_layers * c.dim, in.final_norm = m->final_norm;
+    in.embed = m->embed, in.cos_t = m->cos_t, in.sin_t = m->sin_t;
+    in.kc = m->kv, in.vc = m->kv + (size_t)c.n_layers * c.max_seq * kvd;
+    in.q = m->q, in.logits = m->logits, in.state = m->state, in.prompt = m->prompt, in.out = m->out;
+    if (!tpin) {
+        const int prc = persist::build(in, m->cap_stream, &m->pe);
+        if (prc == FP4X_OK) {
+            m->path = 1;
+        } else if (prc == FP4X_EUNSUPPORTED) {
+            m->pe = nullptr;  // graph path only
+            snprintf(m->persist_why, sizeof(m->persist_why), "%s", fp4x_last_error());
+        } else {
+            rc = prc;
+        }
+    } else {
+        snprintf(m->persist_why, sizeof(m->persist_why), "not built under tensor parallelism");
+    }
+    if (!rc) {
+        const int trc = ptc::build(in, m->cap_stream, &m->pt, tpin);
+        if (trc == FP4X_OK) {
+            m->path = 2;
+        } else if (trc == FP4X_EUNSUPPORTED) {
+            m->pt = nullptr;
+            snprintf(m->tc_why, sizeof(m->tc_why), "%s", fp4x_last_error());
+        } else {
+            rc = trc;
+        }
+    }
+    const char *env = getenv("FP4X_DECODE_PATH");
+    if (env && strcmp(env, "graph") == 0) m->path = 0;
+    if (env && strcmp(env, "persistent") == 0 && m->pe) m->path = 1;
+    return rc;
+}
+
 int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
     FP4X_REQUIRE(cfg && out, "llama_model_create: null pointer");
     FP4X_TRY(validate_config(*cfg));
@@ -383,44 +433,7 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
         return FP4X_OK;
     }
     if (!rc) rc = build_graph(m);
-    if (!rc) {
-        persist::BuildIn in;
-        in.cfg = c;
-        for (auto &L : m->layers) {
-            in.qkv.push_back({L.qkv.w, L.qkv.s, L.qkv.n, L.qkv.k});
-            in.o.push_back({L.o.w, L.o.s, L.o.n, L.o.k});
-            in.gu.push_back({L.gu.w, L.gu.s, L.gu.n, L.gu.k});
-            in.down.push_back({L.down.w, L.down.s, L.down.n, L.down.k});
-        }
-        in.lm = {m->lm_head.w, m->lm_head.s, m->lm_head.n, m->lm_head.k};
-        in.attn_norm = m->norms, in.ffn_norm = m->norms + (size_t)c.n_layers * c.dim, in.final_norm = m->final_norm;
-        in.embed = m->embed, in.cos_t = m->cos_t, in.sin_t = m->sin_t;
-        in.kc = m->kv, in.vc = m->kv + (size_t)c.n_layers * c.max_seq * kvd;
-        in.q = m->q, in.logits = m->logits, in.state = m->state, in.prompt = m->prompt, in.out = m->out;
-        const int prc = persist::build(in, m->cap_stream, &m->pe);
-        if (prc == FP4X_OK) {
-            m->path = 1;
-        } else if (prc == FP4X_EUNSUPPORTED) {
-            m->pe = nullptr;  // graph path only
-            snprintf(m->persist_why, sizeof(m->persist_why), "%s", fp4x_last_error());
-        } else {
-            rc = prc;
-        }
-        if (!rc) {
-            const int trc = ptc::build(in, m->cap_stream, &m->pt);
-            if (trc == FP4X_OK) {
-                m->path = 2;
-            } else if (trc == FP4X_EUNSUPPORTED) {
-                m->pt = nullptr;
-                snprintf(m->tc_why, sizeof(m->tc_why), "%s", fp4x_last_error());
-            } else {
-                rc = trc;
-            }
-        }
-        const char *env = getenv("FP4X_DECODE_PATH");
-        if (env && strcmp(env, "graph") == 0) m->path = 0;
-        if (env && strcmp(env, "persistent") == 0 && m->pe) m->path = 1;
-    }
+    if (!rc) rc = build_persistent(m, nullptr);
     if (rc) return fail(rc);
     *out = m;
     return FP4X_OK;
@@ -642,7 +655,11 @@ extern "C" int llama_model_tp_connect(fp4x_llama_model *m, const void *handles) 
     FP4X_REQUIRE(m->xc, "llama_model_tp_connect: the model was not created with tp_size > 1");
     cudaSetDevice(m->device);
     FP4X_TRY(tp::connect(m->xc, handles));
-    return build_graph(m);
+    FP4X_TRY(build_graph(m));
+    ptc::TpIn t;
+    tp::ptc_buffers(m->xc, t);
+    t.v0 = m->v0;
+    return build_persistent(m, &t);
 }
 
 extern "C" int llama_model_shard(const fp4x_llama_model *m, uint32_t *v0, uint32_t *vocab_local) {

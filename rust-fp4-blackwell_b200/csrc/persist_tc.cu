@@ -144,6 +144,29 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t *p) {
 __device__ __forceinline__ void red_add(float *p, float v) {
     asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
+__device__ __forceinline__ void red_add_sys(float *p, float v) {
+    asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// A row-parallel output element: added into this rank's buffer, and under tensor
+// parallelism into every rank's (peer memory over NVLink).
+__device__ __forceinline__ void add_all_ranks(float *const *bufs, uint32_t ranks, uint32_t i, float v) {
+    if (ranks == 1) {
+        red_add(bufs[0] + i, v);
+    } else {
+        for (uint32_t r = 0; r < ranks; ++r) red_add_sys(bufs[r] + i, v);
+    }
+}
 
 // Bounded mbarrier wait that also gives up when the launch has aborted.
 __device__ bool wait_bar(uint64_t *bar, uint32_t parity, const Params &p, volatile uint32_t *abort) {
@@ -168,6 +191,7 @@ struct Ctx {
     float *red;
     uint32_t nbar;
     uint32_t tsb;  // timestamp slot base of the current layer
+    uint32_t epoch0;  // cross-rank barrier epochs before this launch
     bool ok;
 };
 
@@ -181,7 +205,10 @@ __device__ bool grid_barrier(Ctx &c) {
     c.nbar += 1;
     if (threadIdx.x == 0) {
         if (flag[1]) atomicExch(&p.bar[1], 1u);
-        __threadfence();
+        if (p.tp_size > 1)
+            __threadfence_system();  // this CTA's adds into peer memory are visible before it arrives
+        else
+            __threadfence();
         atomicAdd(&p.bar[0], 1u);
         const uint32_t target = c.nbar * gridDim.x;
         uint32_t ok = 1;
@@ -198,6 +225,33 @@ __device__ bool grid_barrier(Ctx &c) {
                 break;
             }
             __nanosleep(32);
+        }
+        if (ok && p.tp_size > 1) {
+            // cross-rank step: CTA 0 tells every rank this rank's grid arrived, waits for
+            // all ranks, then releases its own CTAs; epochs keep increasing across launches
+            const uint32_t ep = c.epoch0 + c.nbar;
+            if (blockIdx.x == 0) {
+                __threadfence_system();
+                for (uint32_t r = 0; r < p.tp_size; ++r) st_release_sys(p.flagr[r] + 32 * p.tp_rank, ep);
+                for (uint32_t src = 0; src < p.tp_size && ok; ++src)
+                    for (uint32_t i = 0; ld_acquire_sys(p.flagr[p.tp_rank] + 32 * src) < ep; ++i)
+                        if (i > kBarLimit || ld_volatile(&p.bar[1])) {
+                            raise_device_error(DEVERR_FLAG_TIMEOUT);
+                            ok = 0;
+                            break;
+                        }
+                if (!ok) atomicExch(&p.bar[1], 1u);
+                st_release_gpu(&p.bar[2], ok ? ep : 0xFFFFFFFFu);
+            } else {
+                for (uint32_t i = 0; ld_acquire(&p.bar[2]) < ep; ++i) {
+                    if (ld_volatile(&p.bar[1]) || i > kBarLimit) {
+                        if (i > kBarLimit) raise_device_error(DEVERR_FLAG_TIMEOUT);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
         }
         __threadfence();
         flag[0] = ok;
@@ -623,7 +677,7 @@ __device__ void o_projection(Ctx &c, uint32_t lay_count) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (uint32_t i = warp >> 2; i < S.n_pairs; i += kCW / 4) {
         const float s = acc_row(c.tbase, 8 * i);
-        red_add(&p.X[S.pair_tile[i] * 128 + 32 * (warp & 3) + lane], s);
+        add_all_ranks(p.xr, p.tp_size, S.pair_tile[i] * 128 + 32 * (warp & 3) + lane, s);
     }
     CST(10);
 }
@@ -883,7 +937,7 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     const uint32_t mt = p.dim / 128;
     for (uint32_t t = warp >> 2; t < mt; t += kCW / 4) {
         const float s = acc_row(c.tbase, 8 * t);
-        red_add(&p.Y[t * 128 + 32 * (warp & 3) + lane], s);
+        add_all_ranks(p.yr, p.tp_size, t * 128 + 32 * (warp & 3) + lane, s);
     }
     CST(17);
 }
@@ -908,7 +962,8 @@ __device__ void phase_lm(Ctx &c, uint32_t tok_count) {
                 const uint32_t row = S.l_tile[i] * 128 + 32 * (warp & 3) + lane;
                 if (row < p.vocab) {
                     p.logits[row] = s;
-                    if (s > bv || (s == bv && row < bi)) bv = s, bi = row;  // llama_run:283-292
+                    const uint32_t gi = p.v0 + row;  // vocab index (shard offset under TP)
+                    if (s > bv || (s == bv && gi < bi)) bv = s, bi = gi;  // llama_run:283-292
                 }
             }
         }
@@ -928,8 +983,10 @@ __device__ void phase_lm(Ctx &c, uint32_t tok_count) {
         uint32_t ix = ri[0];
         for (int w = 1; w < kCW; ++w)
             if (c.red[128 + w] > v || (c.red[128 + w] == v && ri[w] < ix)) v = c.red[128 + w], ix = ri[w];
-        p.cand_val[blockIdx.x] = v;
-        p.cand_idx[blockIdx.x] = ix;
+        for (uint32_t r = 0; r < p.tp_size; ++r) {  // every rank reduces the same candidate list
+            p.cvr[r][p.tp_rank * gridDim.x + blockIdx.x] = v;
+            p.cir[r][p.tp_rank * gridDim.x + blockIdx.x] = ix;
+        }
     }
 }
 
@@ -1158,6 +1215,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
         c.p = &p, c.S = &S, c.smem = smem, c.L = L, c.B = B, c.tbase = tbase;
         c.red = reinterpret_cast<float *>(smem + L.red);
         c.nbar = 0, c.ok = true;
+        c.epoch0 = p.tp_size > 1 ? *p.epoch : 0u;
         uint32_t tok = p.state[0], pos = pos0;
         const uint32_t n_prompt = p.state[3], cap = p.state[4];
         for (uint32_t it = 0; it < n_eff && c.ok; ++it) {
@@ -1194,7 +1252,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
                 const int lane = threadIdx.x;
                 float bv = -INFINITY;
                 uint32_t bi = 0xFFFFFFFFu;
-                for (uint32_t i = lane; i < gridDim.x; i += 32) {
+                for (uint32_t i = lane; i < gridDim.x * p.tp_size; i += 32) {
                     const float v = __ldcg(&p.cand_val[i]);
                     const uint32_t ix = __ldcg(&p.cand_idx[i]);
                     if (v > bv || (v == bv && ix < bi)) bv = v, bi = ix;
@@ -1223,6 +1281,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
             *B.abort = 1;
             atomicExch(&p.bar[1], 1u);
         }
+        // every rank ran the same barrier sequence: record it for the next launch
+        if (p.tp_size > 1 && c.ok && blockIdx.x == 0 && threadIdx.x == 0) *p.epoch = c.epoch0 + c.nbar;
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -1331,6 +1391,16 @@ static int dalloc(Engine *e, T **p, size_t count) {
     return FP4X_OK;
 }
 
+// Tensor-parallel placement of the kernel's shared buffers (all inside the ranks'
+// exchange areas): this rank, the rank count, its first vocab row, and per rank the
+// X / Y / candidate / flag buffers mapped into this process.
+struct TpIn {
+    uint32_t rank = 0, size = 1, v0 = 0;
+    float *xr[kMaxTp] = {}, *yr[kMaxTp] = {}, *cvr[kMaxTp] = {};
+    uint32_t *cir[kMaxTp] = {}, *flagr[kMaxTp] = {};
+    uint32_t *epoch = nullptr;
+};
+
 #define PTC_UNSUPPORTED(...)            \
     do {                                \
         set_error(__VA_ARGS__);         \
@@ -1340,7 +1410,7 @@ static int dalloc(Engine *e, T **p, size_t count) {
 // Builds the schedule, packs every weight into the per-CTA chunk streams and
 // sizes shared and tensor memory.  FP4X_EUNSUPPORTED when the shape does not
 // fit the kernel's static limits (the caller keeps another path).
-int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
+int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn *tpin = nullptr) {
     const fp4x_llama_config &c = in.cfg;
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     int dev = 0, G = 0, coop = 0, max_smem = 0, cc_major = 0;
@@ -1350,6 +1420,8 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, dev);
     if (!coop || G <= 0) PTC_UNSUPPORTED("tensor-core decode: cooperative launch unavailable");
+    if (tpin && (tpin->size > (uint32_t)kMaxTp || G > 256))
+        PTC_UNSUPPORTED("tensor-core decode: %u ranks x %d SMs above the exchange limits", tpin->size, G);
     if (cc_major != 10) PTC_UNSUPPORTED("tensor-core decode: needs an sm_100 GPU");
     if (c.dim % 128 || c.ffn % 32 || (hd != 64 && hd != 128) || c.n_heads % c.n_kv_heads || c.dim > 8192)
         PTC_UNSUPPORTED("tensor-core decode: unsupported shape");
@@ -1542,15 +1614,23 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
     rc = dalloc(e, &arena, off);
     if (!rc) rc = dalloc(e, &dsched, (size_t)G);
     if (!rc) rc = dalloc(e, &bar, 4);
-    if (!rc) rc = dalloc(e, &X, c.dim);
-    if (!rc) rc = dalloc(e, &Y, c.dim);
+    if (tpin) {  // X, Y and the candidates live in the exchange area
+        X = tpin->xr[tpin->rank], Y = tpin->yr[tpin->rank];
+    } else {
+        if (!rc) rc = dalloc(e, &X, c.dim);
+        if (!rc) rc = dalloc(e, &Y, c.dim);
+    }
     if (!rc) rc = dalloc(e, &qkv, rows_qkv);
     const uint32_t group = c.n_heads / c.n_kv_heads;
     const uint32_t slices = (group == 2 || group == 4 || group == 8) ? (uint32_t)G / c.n_kv_heads : 0u;
     float *apart = nullptr;
     if (!rc && slices) rc = dalloc(e, &apart, (size_t)c.n_heads * slices * (hd + 2));
-    if (!rc) rc = dalloc(e, &cval, (size_t)G);
-    if (!rc) rc = dalloc(e, &cidx, (size_t)G);
+    if (tpin) {
+        cval = tpin->cvr[tpin->rank], cidx = tpin->cir[tpin->rank];
+    } else {
+        if (!rc) rc = dalloc(e, &cval, (size_t)G);
+        if (!rc) rc = dalloc(e, &cidx, (size_t)G);
+    }
     if (!rc) rc = dalloc(e, &djobs, jobs.size());
     if (rc) {
         destroy(e);
@@ -1581,6 +1661,15 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out) {
     P.embed = in.embed, P.cos_t = in.cos_t, P.sin_t = in.sin_t, P.kc = in.kc, P.vc = in.vc;
     P.X = X, P.Y = Y, P.qkv = qkv, P.logits = in.logits, P.cand_val = cval, P.cand_idx = cidx;
     P.attn_part = apart, P.attn_slices = slices;
+    P.tp_rank = 0, P.tp_size = 1, P.v0 = 0, P.epoch = nullptr;
+    P.xr[0] = X, P.yr[0] = Y, P.cvr[0] = cval, P.cir[0] = cidx;
+    if (tpin) {
+        P.tp_rank = tpin->rank, P.tp_size = tpin->size, P.v0 = tpin->v0, P.epoch = tpin->epoch;
+        for (uint32_t r = 0; r < tpin->size; ++r) {
+            P.xr[r] = tpin->xr[r], P.yr[r] = tpin->yr[r], P.cvr[r] = tpin->cvr[r], P.cir[r] = tpin->cir[r];
+            P.flagr[r] = tpin->flagr[r];
+        }
+    }
     P.state = in.state, P.prompt = in.prompt, P.out = in.out, P.bar = bar, P.n_tokens = 0;
     e->p = P;
     e->grid = G;

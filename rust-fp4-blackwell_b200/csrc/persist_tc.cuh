@@ -35,6 +35,7 @@ constexpr int kMaxAUnits = 4;             // QKV (tile, k-range) units per CTA
 constexpr int kMaxPairs = 12;             // (head, O tile) pairs per CTA
 constexpr int kMaxHeads = 4;              // heads attended per CTA
 constexpr int kMaxGroup = 8;              // q heads per KV head (split attention units)
+constexpr int kMaxTp = 8;                 // tensor-parallel ranks
 constexpr uint32_t kSplitMinSeq = 512;    // longer contexts: attention split over (KV head, slice) units
 constexpr int kMaxLm = 8;                 // lm_head tiles per CTA
 constexpr int kMaxBlkPerChunk = 8;
@@ -91,7 +92,14 @@ struct Params {
     const uint32_t *prompt;
     uint32_t *out;
     uint32_t n_tokens;
-    uint32_t *bar;  // [0] grid-barrier counter, [1] abort
+    uint32_t *bar;  // [0] grid-barrier counter, [1] abort, [2] cross-rank release word
+    // tensor parallelism (tp_size 1: xr[0] = X, yr[0] = Y, cvr[0] = cand_val, cir[0] = cand_idx)
+    uint32_t tp_rank, tp_size, v0;             // this rank, ranks, first vocab row of the lm_head shard
+    float *xr[kMaxTp], *yr[kMaxTp];            // every rank's X and Y (row-parallel outputs add into all)
+    float *cvr[kMaxTp];                        // every rank's candidate values [kMaxTp * grid]
+    uint32_t *cir[kMaxTp];                     // ... and indices
+    uint32_t *flagr[kMaxTp];                   // every rank's barrier flags, one 32-word line per source rank
+    uint32_t *epoch;                           // cross-rank barrier epochs done so far (kept across launches)
 };
 
 }  // namespace ptc

@@ -31,8 +31,13 @@ struct Peers {
     uint8_t *area[kMaxRanks];
 };
 
+constexpr uint32_t kMaxCtas = 256;  // argmax candidates per rank (persistent kernel)
+
+// Exchange area of one rank.  The graph path uses slots/flags/arg*; the tensor-core
+// persistent kernel keeps its residual X, FFN delta Y, argmax candidates and
+// barrier flags here so that every rank can add into / write them with peer stores.
 struct Layout {
-    size_t slots, flags, argv, argi, aflags, total;
+    size_t slots, flags, argv, argi, aflags, px, py, pcv, pci, pflag, total;
 };
 
 __host__ __device__ inline Layout layout(uint32_t dim) {
@@ -42,7 +47,12 @@ __host__ __device__ inline Layout layout(uint32_t dim) {
     L.argv = L.flags + 2 * kMaxRanks * 4;
     L.argi = L.argv + 2 * kMaxRanks * 4;
     L.aflags = L.argi + 2 * kMaxRanks * 4;
-    L.total = (L.aflags + 2 * kMaxRanks * 4 + 255) / 256 * 256;
+    L.px = (L.aflags + 2 * kMaxRanks * 4 + 255) / 256 * 256;
+    L.py = L.px + (size_t)dim * 4;
+    L.pcv = L.py + (size_t)dim * 4;
+    L.pci = L.pcv + (size_t)kMaxRanks * kMaxCtas * 4;
+    L.pflag = L.pci + (size_t)kMaxRanks * kMaxCtas * 4;  // one 128-byte line per source rank
+    L.total = (L.pflag + (size_t)kMaxRanks * 128 + 255) / 256 * 256;
     return L;
 }
 
@@ -50,7 +60,7 @@ struct Exchange {
     uint32_t rank = 0, size = 1, dim = 0;
     uint8_t *local = nullptr;  // this rank's area (exported)
     Peers peers = {};          // every rank's area in this process (peers[rank] = local)
-    uint32_t *count = nullptr; // completed exchanges (device)
+    uint32_t *count = nullptr; // completed exchanges (device); [1] = persistent-kernel barrier epoch
     bool connected = false;
 };
 
@@ -246,6 +256,22 @@ int connect(Exchange *x, const void *handles) {
     }
     x->connected = true;
     return FP4X_OK;
+}
+
+// Where the tensor-core persistent kernel finds every rank's X, Y, argmax
+// candidates and barrier flags (inside the exchange areas), and its epoch word.
+void ptc_buffers(const Exchange *x, ptc::TpIn &t) {
+    const Layout L = layout(x->dim);
+    t.rank = x->rank, t.size = x->size;
+    for (uint32_t r = 0; r < x->size; ++r) {
+        uint8_t *base = x->peers.area[r];
+        t.xr[r] = reinterpret_cast<float *>(base + L.px);
+        t.yr[r] = reinterpret_cast<float *>(base + L.py);
+        t.cvr[r] = reinterpret_cast<float *>(base + L.pcv);
+        t.cir[r] = reinterpret_cast<uint32_t *>(base + L.pci);
+        t.flagr[r] = reinterpret_cast<uint32_t *>(base + L.pflag);
+    }
+    t.epoch = x->count + 1;
 }
 
 static int launch_cfg(cudaStream_t st, bool pdl, cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr) {

@@ -33,7 +33,7 @@ def _rel(got, ref):
     return float(np.max(np.abs(got.astype(np.float64) - ref)) / rms)
 
 
-def _worker(rank, world, port, cfg, result):
+def _worker(rank, world, port, cfg, path, result):
     import datetime
     import oracle
     from fp4x import tp
@@ -45,6 +45,7 @@ def _worker(rank, world, port, cfg, result):
     try:
         ref = oracle.Model(cfg)
         m = tp.create_model(cfg)
+        m.set_path(path)
         sh = tp.shard_ranges(cfg, rank, world)
         hd = cfg["head_dim"]
         q0, q1 = sh["heads"][0] * hd, sh["heads"][1] * hd
@@ -94,11 +95,15 @@ def _worker(rank, world, port, cfg, result):
         dist.destroy_process_group()
 
 
-def test_tp2_matches_oracle():
+@pytest.mark.parametrize("path", ["graph", "tensor"])
+def test_tp2_matches_oracle(path):
+    """graph: per-layer kernels + the in-graph peer-memory allreduce kernel;
+    tensor: the persistent tcgen05 kernel adding its row-parallel outputs into every
+    rank's residual over NVLink, with cross-rank grid barriers."""
     world = 2
     with mp.get_context("spawn").Manager() as man:
         result = man.dict()
-        mp.spawn(_worker, args=(world, _free_port(), TINY, result), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), TINY, path, result), nprocs=world, join=True)
         res = dict(result)
     assert set(res) == {0, 1}
     for r, out in res.items():
