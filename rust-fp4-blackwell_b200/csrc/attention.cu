@@ -192,6 +192,246 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
     }
 }
 
+// ---------------------------------------------------------------- tensor-core flash-decode (bf16 caches)
+// A CTA owns (batch b, the HPC q heads of one KV head, one slice of the sequence)
+// like attn_split_kernel, but stages K/V in 64-token tiles with cp.async (16-byte
+// pieces, 128-byte XOR swizzle, a multi-stage ring) and contracts on the tensor
+// cores with mma.sync.m16n8k16 bf16 (f32 accumulate).  Warp w of a tile owns
+// tokens 16w..16w+15:
+//   S^T[token][head] = K[token][:] . q[head][:]  (A = K via ldmatrix, B = q, the
+//     8 mma columns are the (up to 8) heads; q is split into bf16 hi + lo, so an
+//     f32 q keeps ~16 bits and a bf16 q is exact);
+//   online softmax per head over the warp's tokens (f32);
+//   O^T[dim][head] += V^T[dim][token] . P^T[token][head]  (A = V^T via
+//     ldmatrix.trans, B = P written as bf16 hi + lo through shared memory).
+// The 4 warps' states are merged in warp order; slices write (m, l, o) partials
+// for attn_combine_kernel exactly like attn_split_kernel.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *smem_row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(smem_row_addr)));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+}
+
+template <int HD>
+struct MmaCfg {
+    static constexpr int kTile = 64;
+    static constexpr int kStages = HD == 64 ? 4 : 2;
+    static constexpr int kChunks = HD / 8;  // 16-byte pieces per row
+    static constexpr size_t kStageElems = (size_t)kTile * HD;
+    static constexpr size_t kSmem = (size_t)kStages * 2 * kStageElems * 2  // K and V ring
+                                    + (size_t)4 * 2 * 8 * 16 * 2            // P^T hi/lo per warp
+                                    + (size_t)4 * 8 * (HD + 2) * 4;         // warp merge
+};
+
+// 16-byte piece c of tile row r, swizzled within groups of 8 pieces.
+template <int HD>
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
+    return r * HD + (((c & ~7u) | ((c ^ r) & 7u)) * 8u);
+}
+
+template <int HD, int HPC, typename QT, typename OT>
+__global__ void __launch_bounds__(kThreads) attn_mma_kernel(Params p) {
+    using C = MmaCfg<HD>;
+    constexpr int NT = HD / 16;
+    extern __shared__ __align__(128) uint8_t sm_raw[];
+    uint16_t *ks = reinterpret_cast<uint16_t *>(sm_raw);
+    uint16_t *vs = ks + C::kStages * C::kStageElems;
+    uint16_t *ps = vs + C::kStages * C::kStageElems;          // [warp][hi|lo][head 8][token 16]
+    float *mrg = reinterpret_cast<float *>(ps + 4 * 2 * 8 * 16);  // [warp][head 8][HD + 2]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t split = blockIdx.x, hgrp = blockIdx.y, b = blockIdx.z;
+    const uint32_t h0 = hgrp * HPC;
+    const uint32_t group = p.n_heads / p.n_kv, kvh = h0 / group;
+    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
+    const uint32_t t_begin = split * p.split_len, t_end = min(seq, t_begin + p.split_len);
+    if (t_begin >= seq) return;
+    const size_t row_stride = (size_t)p.n_kv * HD;
+    const uint16_t *kbase = reinterpret_cast<const uint16_t *>(p.kc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
+    const uint16_t *vbase = reinterpret_cast<const uint16_t *>(p.vc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
+
+    // q fragments (B operand, column n = head g): dims 16kk + 2t (+1), +8
+    uint32_t qh[NT][2], ql[NT][2];
+    {
+        const QT *q = reinterpret_cast<const QT *>(p.q) + ((size_t)b * p.n_heads + h0) * HD;
+#pragma unroll
+        for (int kk = 0; kk < NT; ++kk)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                float q0 = 0.0f, q1 = 0.0f;
+                if (g < HPC) {
+                    q0 = to_f32(q[g * HD + 16 * kk + 8 * r + 2 * t]);
+                    q1 = to_f32(q[g * HD + 16 * kk + 8 * r + 2 * t + 1]);
+                }
+                const float h0f = bf16_bits_to_f32(f32_to_bf16_bits(q0)), h1f = bf16_bits_to_f32(f32_to_bf16_bits(q1));
+                qh[kk][r] = pack_bf16x2(q0, q1);
+                ql[kk][r] = pack_bf16x2(q0 - h0f, q1 - h1f);
+            }
+    }
+    const uint32_t ntiles = (t_end - t_begin + C::kTile - 1) / C::kTile;
+    auto load_tile = [&](uint32_t i) {
+        const uint32_t st = i % C::kStages, t0 = t_begin + i * C::kTile;
+        uint16_t *kd = ks + st * C::kStageElems, *vd = vs + st * C::kStageElems;
+        for (uint32_t idx = tid; idx < (uint32_t)C::kTile * C::kChunks; idx += kThreads) {
+            const uint32_t r = idx / C::kChunks, c = idx % C::kChunks, tok = t0 + r;
+            const bool valid = tok < t_end;
+            const size_t src = (size_t)(valid ? tok : t_begin) * row_stride + 8 * c;
+            cp_async16(kd + swz<HD>(r, c), kbase + src, valid);
+            cp_async16(vd + swz<HD>(r, c), vbase + src, valid);
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < C::kStages - 1; ++i) {
+        if ((uint32_t)i < ntiles) load_tile(i);
+        cp_async_commit();
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads 2t, 2t+1
+    float o[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    uint16_t *pw = ps + warp * (2 * 8 * 16);
+    for (uint32_t i = 0; i < ntiles; ++i) {
+        if (i + C::kStages - 1 < ntiles) load_tile(i + C::kStages - 1);
+        cp_async_commit();
+        cp_async_wait<C::kStages - 1>();
+        __syncthreads();
+        const uint32_t st = i % C::kStages, t0 = t_begin + i * C::kTile;
+        const uint16_t *kt = ks + st * C::kStageElems, *vt = vs + st * C::kStageElems;
+        // S^T for tokens 16w..16w+15
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t arow = 16 * warp + (lane & 15);
+#pragma unroll
+        for (int kk = 0; kk < NT; ++kk) {
+            uint32_t a[4];
+            ldmatrix_x4(a, kt + swz<HD>(arow, 2 * kk + (lane >> 4)));
+            mma_bf16_16816(s, a, qh[kk][0], qh[kk][1], s);
+            mma_bf16_16816(s, a, ql[kk][0], ql[kk][1], s);
+        }
+        const uint32_t tokA = t0 + 16 * warp + g, tokB = tokA + 8;
+        const float sa0 = tokA < t_end ? s[0] * p.scale : -INFINITY, sa1 = tokA < t_end ? s[1] * p.scale : -INFINITY;
+        const float sb0 = tokB < t_end ? s[2] * p.scale : -INFINITY, sb1 = tokB < t_end ? s[3] * p.scale : -INFINITY;
+        float mx0 = fmaxf(sa0, sb0), mx1 = fmaxf(sa1, sb1);
+#pragma unroll
+        for (int o2 = 4; o2 < 32; o2 <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o2));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        // a warp whose tokens are all masked keeps -inf: guard the exponent base
+        const float base0 = mn0 == -INFINITY ? 0.0f : mn0, base1 = mn1 == -INFINITY ? 0.0f : mn1;
+        const float al0 = __expf(m0 - base0), al1 = __expf(m1 - base1);
+        const float pa0 = __expf(sa0 - base0), pa1 = __expf(sa1 - base1);
+        const float pb0 = __expf(sb0 - base0), pb1 = __expf(sb1 - base1);
+        float sum0 = pa0 + pb0, sum1 = pa1 + pb1;
+#pragma unroll
+        for (int o2 = 4; o2 < 32; o2 <<= 1) {
+            sum0 += __shfl_xor_sync(0xffffffffu, sum0, o2);
+            sum1 += __shfl_xor_sync(0xffffffffu, sum1, o2);
+        }
+        l0 = l0 * al0 + sum0, l1 = l1 * al1 + sum1;
+        m0 = mn0, m1 = mn1;
+#pragma unroll
+        for (int dm = 0; dm < NT; ++dm) o[dm][0] *= al0, o[dm][1] *= al1, o[dm][2] *= al0, o[dm][3] *= al1;
+        // P^T -> shared as [head][token] bf16 hi and lo
+        {
+            const float pv[4] = {pa0, pa1, pb0, pb1};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t head = 2 * t + (j & 1), tok = g + 8 * (j >> 1);
+                const uint16_t hi = f32_to_bf16_bits(pv[j]);
+                pw[head * 16 + tok] = hi;
+                pw[128 + head * 16 + tok] = f32_to_bf16_bits(pv[j] - bf16_bits_to_f32(hi));
+            }
+        }
+        __syncwarp();
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(pw + g * 16 + 2 * t);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(pw + g * 16 + 2 * t + 8);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(pw + 128 + g * 16 + 2 * t);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(pw + 128 + g * 16 + 2 * t + 8);
+        // O^T += V^T P^T
+        const uint32_t vrow = 16 * warp + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+        for (int dm = 0; dm < NT; ++dm) {
+            uint32_t a[4];
+            ldmatrix_x4_trans(a, vt + swz<HD>(vrow, 2 * dm + ((lane >> 3) & 1)));
+            mma_bf16_16816(o[dm], a, bh0, bh1, o[dm]);
+            mma_bf16_16816(o[dm], a, bl0, bl1, o[dm]);
+        }
+        __syncthreads();  // the stage is reloaded next iteration
+    }
+    // merge the 4 warps (fixed order): rows of o = dims 16dm + g (+8), columns = heads 2t, 2t+1
+    float *mw = mrg + warp * 8 * (HD + 2);
+    if (g == 0) {
+        mw[(2 * t) * (HD + 2)] = m0, mw[(2 * t) * (HD + 2) + 1] = l0;
+        mw[(2 * t + 1) * (HD + 2)] = m1, mw[(2 * t + 1) * (HD + 2) + 1] = l1;
+    }
+#pragma unroll
+    for (int dm = 0; dm < NT; ++dm) {
+        mw[(2 * t) * (HD + 2) + 2 + 16 * dm + g] = o[dm][0];
+        mw[(2 * t + 1) * (HD + 2) + 2 + 16 * dm + g] = o[dm][1];
+        mw[(2 * t) * (HD + 2) + 2 + 16 * dm + g + 8] = o[dm][2];
+        mw[(2 * t + 1) * (HD + 2) + 2 + 16 * dm + g + 8] = o[dm][3];
+    }
+    __syncthreads();
+    for (uint32_t i = tid; i < HPC * HD; i += kThreads) {
+        const uint32_t h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mrg[(w * 8 + h) * (HD + 2)]);
+        float L = 0.0f, O = 0.0f;
+        for (int w = 0; w < kWarps; ++w) {
+            const float *r = mrg + (w * 8 + h) * (HD + 2);
+            const float f = r[0] == -INFINITY ? 0.0f : __expf(r[0] - M);
+            L += r[1] * f;
+            O += r[2 + d] * f;
+        }
+        const size_t bh = (size_t)b * p.n_heads + h0 + h;
+        if (p.splits == 1) {
+            store_out(reinterpret_cast<OT *>(p.out) + bh * HD + d, O / L);
+        } else {
+            float *rec = p.ws + (bh * p.splits + split) * (HD + 2);
+            rec[2 + d] = O;
+            if (d == 0) rec[0] = M, rec[1] = L;
+        }
+    }
+}
+
+template <int HD, int HPC, typename QT, typename OT>
+cudaError_t launch_mma(cudaStream_t stream, const Params &p, dim3 grid, bool pdl) {
+    using C = MmaCfg<HD>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        const cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, HPC, QT, OT>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_mma_kernel<HD, HPC, QT, OT>, p);
+}
+
 // grid = (n_heads, batch), block = HD: merge the slices of one (b, head).
 template <int HD, typename OT>
 __global__ void attn_combine_kernel(Params p) {
@@ -258,6 +498,22 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
     p.q = q, p.kc = kc, p.vc = vc, p.out = out, p.ws = static_cast<float *>(ws);
     p.pos_ptr = nullptr;
     dim3 grid(p.splits, n_heads / hpc, batch);
+    if (sizeof(KT) == 2 && (hpc == 4 || hpc == 8)) {
+        cudaError_t e = cudaSuccess;
+        if (hd == 64 && hpc == 8) e = launch_mma<64, 8, QT, OT>(stream, p, grid, false);
+        if (hd == 64 && hpc == 4) e = launch_mma<64, 4, QT, OT>(stream, p, grid, false);
+        if (hd == 128 && hpc == 8) e = launch_mma<128, 8, QT, OT>(stream, p, grid, false);
+        if (hd == 128 && hpc == 4) e = launch_mma<128, 4, QT, OT>(stream, p, grid, false);
+        if (e != cudaSuccess) {
+            set_error("llama_attn_decode: %s", cudaGetErrorString(e));
+            return FP4X_ECUDA;
+        }
+        if (p.splits > 1) {
+            if (hd == 64) attn_combine_kernel<64, OT><<<dim3(n_heads, batch), 64, 0, stream>>>(p);
+            else attn_combine_kernel<128, OT><<<dim3(n_heads, batch), 128, 0, stream>>>(p);
+        }
+        return check_launch("llama_attn_decode");
+    }
 #define FP4X_ATTN_CASE(HD_, HPC_)                                                                       \
     if (hd == HD_ && hpc == HPC_) {                                                                   \
         attn_split_kernel<HD_, HPC_, QT, KT, OT><<<grid, kThreads, 0, stream>>>(p);                   \
@@ -287,7 +543,8 @@ int launch_engine_t(cudaStream_t stream, const Params &p, bool pdl) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_split_kernel<HD, HPC, float, uint16_t, float>, p);
+    cudaError_t e = (HPC == 4 || HPC == 8) ? launch_mma<HD, HPC, float, float>(stream, p, cfg.gridDim, pdl)
+                                            : cudaLaunchKernelEx(&cfg, attn_split_kernel<HD, HPC, float, uint16_t, float>, p);
     if (e == cudaSuccess && p.splits > 1) {
         cudaLaunchConfig_t c2 = cfg;
         c2.gridDim = dim3(p.n_heads, p.batch);
