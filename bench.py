@@ -411,6 +411,60 @@ def run_config4(args):
     return 0
 
 
+def run_batch(args):
+    """Batched decode through the llama_batch engine (every linear on the tcgen05
+    fp4_mma GEMM, 8-term MXFP4 activations): BASELINE config 4 at batch 64
+    (--batch-model llama8b --batch-ctx 4096) or the TinyLlama shape.  Every
+    sequence starts at a context of --batch-ctx positions of zero-filled KV cache
+    (prefill not timed); step = one token of every sequence; value = tokens of
+    all sequences / device time.  Bytes per step = MXFP4 weights + the bf16 K/V
+    rows every sequence reads (at the mean position of the timed steps)."""
+    import torch
+    from fp4x import engine
+    torch.cuda.set_device(0)
+    base = engine.LLAMA3_8B if args.batch_model == "llama8b" else engine.TINYLLAMA
+    B, ctx = args.batch, args.batch_ctx
+    cfg = dict(base, max_seq=ctx + args.warmup + args.steps + 8)
+    m = engine.Model(cfg)
+    b = engine.Batch(m, B)
+    for s in range(B):
+        b.set_length(s, ctx, (17 + 31 * s) % cfg["vocab"])
+    b.decode(args.warmup)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record(st)
+        b.decode(args.steps)
+        e1.record(st)
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) * 1e-3
+    wbytes = m.weight_bytes()
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    mean_seq = ctx + args.warmup + (args.steps + 1) / 2
+    kv_bytes = B * mean_seq * cfg["n_layers"] * kvd * 2 * 2
+    per_step = t / args.steps
+    peak, peak_kind = hbm_peak()
+    b.close()
+    m.close()
+    line = {"metric": f"batched MXFP4 decode tok/s ({args.batch_model} shape, batch {B})", "value": B * args.steps / t,
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "mxf4 x mxf4(8-term) -> f32", "data": "synthetic (seeded N(0,0.02) weights -> MXFP4)",
+            "config": {"workload": "config4-batch" if args.batch_model == "llama8b" else "tinyllama-batch",
+                       "batch": B, "context": ctx,
+                       "kv": "zero-filled cache of ctx positions per sequence (prefill not timed)",
+                       "l2": "weights and KV caches far above L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "kernel": "batched decode step (fp4_mma + attention)",
+                         "achieved": (wbytes + kv_bytes) / per_step / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": (wbytes + kv_bytes) / per_step / 1e9 / peak,
+                         "bytes_per_step": wbytes + kv_bytes, "weight_bytes": wbytes, "kv_bytes": kv_bytes,
+                         "peak_kind": peak_kind},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def gemv_config0(torch, peak):
     """Config 0 GEMV (fp4_gemv through the C ABI) over 64 rotated weight copies,
     captured in one CUDA graph (no host launch gaps), CUDA-event timed."""
@@ -466,6 +520,9 @@ def main():
     ap.add_argument("--c2-ctx", default="512,2048,8192,32768")
     ap.add_argument("--c2-batch", default="1,8,64")
     ap.add_argument("--c3-linears", default=",".join(C3_LINEARS))
+    ap.add_argument("--batch", type=int, default=0, help="batched decode of this many sequences instead")
+    ap.add_argument("--batch-model", default="llama8b", choices=["llama8b", "tinyllama"])
+    ap.add_argument("--batch-ctx", type=int, default=4096)
     args = ap.parse_args()
     assert args.warmup >= 3, "timing rules: at least 3 warm-up steps"
     if args.impl == "reference":
@@ -476,6 +533,8 @@ def main():
         return run_config2(args)
     if args.config4:
         return run_config4(args)
+    if args.batch:
+        return run_batch(args)
 
     import torch
     rank = int(os.environ.get("RANK", "0"))

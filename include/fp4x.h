@@ -267,6 +267,38 @@ FP4X_API uint32_t llama_model_kernels_per_token(const fp4x_llama_model *m);
 /* MXFP4 bytes (packed + scales) streamed per token (all linears incl. lm_head). */
 FP4X_API size_t llama_model_weight_bytes(const fp4x_llama_model *m);
 
+/* ---- Batched engine (BASELINE config 4 at batch 64; batched prompt prefill).
+ * The reference decodes one sequence and prefills token by token
+ * (llama_run/src/main.rs:544-587); here `rows` sequences with their own bf16 KV
+ * caches ([layer][rows][max_seq][kvd]) run through the model's weights together,
+ * every linear layer on the tcgen05 fp4_mma GEMM (activations as 8-term MXFP4
+ * sums, fp32 accumulation).  Single GPU (tp_size 1).  The model handle must
+ * outlive the batch. */
+typedef struct fp4x_llama_batch fp4x_llama_batch;
+FP4X_API int llama_batch_create(fp4x_llama_model *m, uint32_t rows /* 1..256 */, fp4x_llama_batch **out);
+FP4X_API int llama_batch_destroy(fp4x_llama_batch *b);
+/* Prefill n prompt tokens (HOST array) of sequence `seq` after its current
+ * length, up to `rows` tokens per pass, each attending causally; the argmax of
+ * the last one becomes the sequence's next token. */
+FP4X_API int llama_batch_prefill(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t seq, const uint32_t *tokens,
+                                 uint32_t n);
+/* Declare sequence `seq` to hold `len` cached positions (whatever the cache
+ * holds there, zeros after creation) with `next_token` at position len: a
+ * context set-up for throughput runs without a prefill. */
+FP4X_API int llama_batch_set_length(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t seq, uint32_t len,
+                                    uint32_t next_token);
+/* n_steps greedy decode steps of all `rows` sequences (one CUDA graph each). */
+FP4X_API int llama_batch_decode(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t n_steps);
+/* Token history of sequence `seq` (positions 0..len-1, the last one the next
+ * token to be consumed) to a HOST array; *len_out gets len.  Synchronous. */
+FP4X_API int llama_batch_tokens(fp4x_llama_batch *b, uint32_t seq, uint32_t *out_host, uint32_t n,
+                                uint32_t *len_out);
+/* Logits of the last pass to a HOST array [*rows_out][vocab] (decode: one row
+ * per sequence; prefill: the last prompt token).  Synchronous. */
+FP4X_API int llama_batch_logits(fp4x_llama_batch *b, float *logits_host, uint32_t *rows_out);
+/* Bytes of the batch's KV caches. */
+FP4X_API size_t llama_batch_kv_bytes(const fp4x_llama_batch *b);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
     constexpr uint32_t H = HPC;
     const uint32_t h0 = hgrp * H;
     const uint32_t group = p.n_heads / p.n_kv, kvh = h0 / group;
-    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
+    const uint32_t seq = seq_of(p, b);
     const uint32_t t_begin = split * p.split_len, t_end = min(seq, t_begin + p.split_len);
     if (t_begin >= seq) return;  // slice past the current position (whole CTA, before any barrier)
 
@@ -93,8 +93,8 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(Params p) {
     __syncthreads();
 
     const size_t row_stride = (size_t)p.n_kv * HD;
-    const KT *kbase = reinterpret_cast<const KT *>(p.kc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
-    const KT *vbase = reinterpret_cast<const KT *>(p.vc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
+    const KT *kbase = reinterpret_cast<const KT *>(p.kc) + cache_of(p, b) * p.max_seq * row_stride + (size_t)kvh * HD;
+    const KT *vbase = reinterpret_cast<const KT *>(p.vc) + cache_of(p, b) * p.max_seq * row_stride + (size_t)kvh * HD;
 
     float m[HPC], l[HPC], o[HPC][NV];
 #pragma unroll
@@ -257,12 +257,12 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(Params p) {
     const uint32_t split = blockIdx.x, hgrp = blockIdx.y, b = blockIdx.z;
     const uint32_t h0 = hgrp * HPC;
     const uint32_t group = p.n_heads / p.n_kv, kvh = h0 / group;
-    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
+    const uint32_t seq = seq_of(p, b);
     const uint32_t t_begin = split * p.split_len, t_end = min(seq, t_begin + p.split_len);
     if (t_begin >= seq) return;
     const size_t row_stride = (size_t)p.n_kv * HD;
-    const uint16_t *kbase = reinterpret_cast<const uint16_t *>(p.kc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
-    const uint16_t *vbase = reinterpret_cast<const uint16_t *>(p.vc) + (size_t)b * p.max_seq * row_stride + (size_t)kvh * HD;
+    const uint16_t *kbase = reinterpret_cast<const uint16_t *>(p.kc) + cache_of(p, b) * p.max_seq * row_stride + (size_t)kvh * HD;
+    const uint16_t *vbase = reinterpret_cast<const uint16_t *>(p.vc) + cache_of(p, b) * p.max_seq * row_stride + (size_t)kvh * HD;
 
     // q fragments (B operand, column n = head g): dims 16kk + 2t (+1), +8
     uint32_t qh[NT][2], ql[NT][2];
@@ -440,7 +440,7 @@ __global__ void attn_combine_kernel(Params p) {
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const size_t bh = (size_t)b * p.n_heads + h;
     const float *rec = p.ws + bh * p.splits * (HD + 2);
-    const uint32_t seq = p.pos_ptr ? min(*p.pos_ptr + 1, p.max_seq) : p.seq;
+    const uint32_t seq = seq_of(p, b);
     const uint32_t used = (seq + p.split_len - 1) / p.split_len;
     float M = -INFINITY;
     for (uint32_t s = 0; s < used; ++s) M = fmaxf(M, rec[s * (HD + 2)]);

@@ -10,3 +10,4 @@
 #include "persist_tc.cu"
 #include "tp.cu"
 #include "engine.cu"
+#include "batch.cu"

@@ -88,8 +88,9 @@ __host__ __device__ inline Geo geometry(uint32_t nt) {
 struct Args {
     uint32_t m, n, k, nt, kps;  // kps: K stages per split
     const uint8_t *sa, *sw;     // scales [m][k/32], [n][k/32]
-    void *d;                    // [m][n] bf16 or f32
+    void *d;                    // [m / terms][n] bf16 or f32
     uint32_t mode;
+    uint32_t terms;             // 1, or 8: A rows 8t..8t+7 are the MXFP4 terms of token t (summed)
 };
 
 // Bounded wait that also gives up when another role of the CTA has aborted.
@@ -233,6 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[8];
                 tc::tmem_ld_x8(tbase + ((32 * q) << 16) + c0, v);
                 tc::tmem_wait_ld();
+                if (a.terms == 8) {  // the 8 columns are the terms of one token: add them
+                    const uint32_t tok = (tok0 + c0) >> 3;
+                    if (!row_ok || 8 * tok >= a.m) continue;
+                    float sum = v[0];
+#pragma unroll
+                    for (uint32_t j = 1; j < 8; ++j) sum += v[j];
+                    const size_t o = (size_t)tok * a.n + row;
+                    if (a.mode == OUT_BF16)
+                        reinterpret_cast<uint16_t *>(a.d)[o] = f32_to_bf16_bits(sum);
+                    else if (a.mode == OUT_F32)
+                        reinterpret_cast<float *>(a.d)[o] = sum;
+                    else
+                        atomicAdd(reinterpret_cast<float *>(a.d) + o, sum);
+                    continue;
+                }
 #pragma unroll
                 for (uint32_t j = 0; j < 8; ++j) {
                     const uint32_t tok = tok0 + c0 + j;
@@ -354,7 +370,7 @@ int validate(uint32_t m, uint32_t n, uint32_t k, const void *a, const void *sa, 
 }
 
 int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa,
-           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p) {
+           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms = 1) {
     CUtensorMap map_w, map_a;
     if (!tc::make_map_sw128(&map_w, w, k / 2, n, 128) || !tc::make_map_sw128(&map_a, a, k / 2, m, p.nt)) {
         set_error("fp4_mma: cuTensorMapEncodeTiled failed (m=%u n=%u k=%u)", m, n, k);
@@ -370,7 +386,7 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
         set_error("fp4_mma: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
         return FP4X_ECUDA;
     }
-    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode};
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms};
     mxf4_gemm_kernel<<<dim3(p.m_tiles, p.n_tiles, p.splits), kThreads, p.g.smem, s>>>(map_w, map_a, args);
     return check_launch("fp4_mma");
 }

@@ -321,8 +321,12 @@ __device__ __forceinline__ uint32_t pack_e2m1x8(const float (&y)[8]) {
 // residual after term 1 within 2^e1 and after each later term within half its
 // scale, so every term stays inside +-6 and the 8-term sum equals the input to
 // 2^(e1-21) (~1.6e-7 of the block maximum); every step is exact in fp32.
-__device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint32_t w, bool valid, uint8_t *B,
-                                                uint8_t *sfb, bool pairs) {
+// Exponent of term t of a block whose first-term exponent is e1.
+__device__ __forceinline__ int term_exp(int e1, int t) { return max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t)); }
+
+// The terms themselves: words[t] = the 8 E2M1 codes of term t for x[] (x is
+// consumed); returns e1.  The block maximum is taken over lanes l, l^1, l^2.
+__device__ __forceinline__ int term_words8(float (&x)[8], uint32_t (&words)[8]) {
     float a = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(x[j]));
@@ -331,10 +335,9 @@ __device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint3
     const uint32_t bits = __float_as_uint(a);
     int e1 = (int)((bits >> 23) & 0xFFu) - 127;
     e1 = (bits & 0x7FFFFFu) <= 0x400000u ? e1 - 2 : e1 - 1;
-    uint32_t words[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        const int e = max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t));
+        const int e = term_exp(e1, t);
         const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
         const float s = __uint_as_float((uint32_t)(127 + e) << 23);
         float y[8];
@@ -349,6 +352,13 @@ __device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint3
             x[2 * j + 1] = fmaf(-__high2float(q), s, x[2 * j + 1]);
         }
     }
+    return e1;
+}
+
+__device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint32_t w, bool valid, uint8_t *B,
+                                                uint8_t *sfb, bool pairs) {
+    uint32_t words[8];
+    const int e1 = term_words8(x, words);
     if (!valid) return;
     // term order rotated by block: the 8 blocks of a warp (128 bytes apart) then hit
     // 8 different bank groups instead of one
@@ -363,7 +373,7 @@ __device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint3
     if (w == 0) {
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-            const uint8_t sb = (uint8_t)(max(-126, min(125, t == 0 ? e1 : e1 + 1 - 3 * t)) + 127);
+            const uint8_t sb = (uint8_t)(term_exp(e1, t) + 127);
             if (!pairs) {
                 sfb[(b >> 2) * 128 + t * 16 + (b & 3)] = sb;
             } else {

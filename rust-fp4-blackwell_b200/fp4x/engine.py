@@ -47,6 +47,14 @@ SIGNATURES = {
     "llama_model_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "llama_model_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "llama_model_shard": (C.c_int, [C.c_void_p, _u32p, _u32p]),
+    "llama_batch_create": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "llama_batch_destroy": (C.c_int, [C.c_void_p]),
+    "llama_batch_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, _u32p, C.c_uint32]),
+    "llama_batch_set_length": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "llama_batch_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "llama_batch_tokens": (C.c_int, [C.c_void_p, C.c_uint32, _u32p, C.c_uint32, _u32p]),
+    "llama_batch_logits": (C.c_int, [C.c_void_p, _f32p, _u32p]),
+    "llama_batch_kv_bytes": (C.c_size_t, [C.c_void_p]),
 }
 
 
@@ -169,3 +177,61 @@ class Model:
 
     def weight_bytes(self) -> int:
         return int(self.L.llama_model_weight_bytes(self._h))
+
+
+class Batch:
+    """Batched engine over a Model's weights (llama_batch_*): `rows` sequences
+    with their own KV caches, decoded together; prompts prefilled `rows` tokens
+    per pass.  Every linear runs on the tcgen05 fp4_mma GEMM."""
+
+    def __init__(self, model: Model, rows: int):
+        self.m = model
+        self.L = model.L
+        self.rows = rows
+        h = C.c_void_p()
+        check(self.L.llama_batch_create(model._h, rows, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.L.llama_batch_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, seq: int, tokens):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        check(self.L.llama_batch_prefill(self._h, self.m._st(), seq, _p(t, C.c_uint32), len(t)))
+
+    def set_length(self, seq: int, length: int, next_token: int = 0):
+        check(self.L.llama_batch_set_length(self._h, self.m._st(), seq, length, next_token))
+
+    def decode(self, n_steps: int):
+        check(self.L.llama_batch_decode(self._h, self.m._st(), n_steps))
+
+    def tokens(self, seq: int):
+        n = C.c_uint32(0)
+        check(self.L.llama_batch_tokens(self._h, seq, None, 0, C.byref(n)))
+        out = np.zeros(n.value, np.uint32)
+        check(self.L.llama_batch_tokens(self._h, seq, _p(out, C.c_uint32), n.value, None))
+        return out
+
+    def logits(self):
+        r = C.c_uint32(0)
+        check(self.L.llama_batch_logits(self._h, None, C.byref(r)))
+        out = np.empty((r.value, self.m.shard()[1]), np.float32)
+        check(self.L.llama_batch_logits(self._h, _p(out, C.c_float), None))
+        return out
+
+    def kv_bytes(self) -> int:
+        return int(self.L.llama_batch_kv_bytes(self._h))
