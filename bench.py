@@ -434,10 +434,14 @@ def run_batch(args):
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clk:
+        if args.profile_region:
+            torch.cuda.profiler.start()
         e0.record(st)
         b.decode(args.steps)
         e1.record(st)
         torch.cuda.synchronize()
+        if args.profile_region:
+            torch.cuda.profiler.stop()
     t = e0.elapsed_time(e1) * 1e-3
     wbytes = m.weight_bytes()
     kvd = cfg["n_kv_heads"] * cfg["head_dim"]
@@ -523,6 +527,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="batched decode of this many sequences instead")
     ap.add_argument("--batch-model", default="llama8b", choices=["llama8b", "tinyllama"])
     ap.add_argument("--batch-ctx", type=int, default=4096)
+    ap.add_argument("--profile-region", action="store_true",
+                    help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = ap.parse_args()
     assert args.warmup >= 3, "timing rules: at least 3 warm-up steps"
     if args.impl == "reference":
