@@ -106,13 +106,16 @@ FP4X_API int fp4_gemv_f32x(fp4x_stream_t stream, uint32_t n, uint32_t k, const u
  * fp4_mma_allones (examples/fp4_mma/src/main.rs:18-54, sm_120a mma.sync); this
  * is the batched-decode / prefill GEMM built on it.  k must be a multiple of 64;
  * a and w 16-byte aligned.  When the tile grid is too small to fill the GPU the
- * K range is split and partial sums meet in an fp32 workspace of
- * fp4_mma_workspace_size(m, n, k) bytes (0 = none needed; may then be NULL). */
+ * K range is split: each split writes fp32 partial sums to the workspace and the
+ * last CTA of a tile to finish adds them in split order (deterministic), so the
+ * workspace holds fp4_mma_workspace_size(m, n, k) bytes (0 = none needed; may
+ * then be NULL). */
 FP4X_API size_t fp4_mma_workspace_size(uint32_t m, uint32_t n, uint32_t k);
 FP4X_API int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
                      const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, uint16_t *d_bf16,
                      void *workspace, size_t workspace_bytes);
-/* Same GEMM with fp32 output (exact accumulator values; no workspace). */
+/* Same GEMM with fp32 output (exact accumulator values; no workspace, so no
+ * K split: one CTA per output tile). */
 FP4X_API int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
                          const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float *d);
 /* The reference's known-answer test on the tcgen05 path: A = B = all 1.0

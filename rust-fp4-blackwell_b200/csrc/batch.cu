@@ -50,7 +50,10 @@ struct fp4x_llama_batch {
     float *logits = nullptr; // [rows][vocab]
     float *attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
-    uint8_t *act = nullptr, *act_s = nullptr;  // term rows [8 rows][kmax / 2], [8 rows][kmax / 32]
+    uint32_t terms = 4;      // MXFP4 terms per activation row (4 or 8)
+    uint8_t *act = nullptr, *act_s = nullptr;  // term rows [terms rows][kmax / 2], [terms rows][kmax / 32]
+    float *mma_part = nullptr;  // split-K partials
+    size_t mma_part_bytes = 0;
     uint32_t *dec_tok = nullptr, *dec_pos = nullptr;            // per sequence: next token, its position
     uint32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_cache = nullptr;  // prefill rows
     uint32_t *prompt = nullptr;  // staging for prefill tokens [max_seq]
@@ -67,7 +70,7 @@ namespace batch {
 
 using engine::cuda_fail;
 
-constexpr uint32_t kTerms = 8;
+constexpr uint32_t kMaxTerms = 8;
 constexpr int kThreads = 256;
 
 enum Src : int { SRC_EMBED = 0, SRC_NORM = 1, SRC_PLAIN = 2, SRC_SWIGLU = 3 };
@@ -112,93 +115,97 @@ __device__ __forceinline__ void load8(float (&x)[8], uint32_t i, uint32_t r, uin
     }
 }
 
-// Row r of the source -> (RMSNorm) -> 8 term rows 8r..8r+7 of act (packed E2M1,
+// Row r of the source -> (RMSNorm) -> term rows T r .. T r + T - 1 of act (packed E2M1,
 // low nibble = lower k) + act_s (E8M0 per 32).  Thread = one 8-value word; the 4
-// words of a 32-block sit in adjacent lanes.  SRC_EMBED also writes the gathered
-// row to x_out; SRC_SWIGLU clears the gate/up row it consumed.
+// words of a 32-block sit in adjacent lanes; CTA (r, c) covers words
+// [c * kThreads, (c + 1) * kThreads) of the row (the RMSNorm sum of squares is
+// taken over the whole row by every CTA of it).  SRC_EMBED also writes the
+// gathered row to x_out; SRC_SWIGLU clears the gate/up values it consumed.
 template <int SRC>
 __global__ void __launch_bounds__(kThreads) rows_decompose_kernel(uint32_t K, const float *src, float *x_out,
                                                                   const uint16_t *embed, const uint32_t *tok,
                                                                   const float *norm_w, float eps, uint8_t *act,
-                                                                  uint8_t *act_s, uint32_t row0) {
+                                                                  uint8_t *act_s, uint32_t row0, uint32_t terms) {
     __shared__ float red[kThreads / 32];
     const uint32_t r = blockIdx.x, rs = row0 + r;  // output row, source row
-    const uint32_t nw = K / 8, lane = threadIdx.x & 31;
+    const uint32_t nw = K / 8, i = blockIdx.y * kThreads + threadIdx.x;
     const uint16_t *erow = SRC == SRC_EMBED ? embed + (size_t)tok[rs] * K : nullptr;
     float rms = 1.0f;
     if (SRC == SRC_EMBED || SRC == SRC_NORM) {
         float ss = 0.0f;
-        for (uint32_t i = threadIdx.x; i < nw; i += kThreads) {
+        for (uint32_t j = threadIdx.x; j < nw; j += kThreads) {
             float x[8];
-            load8<SRC>(x, i, rs, K, src, erow);
+            load8<SRC>(x, j, rs, K, src, erow);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
-            if (SRC == SRC_EMBED) {
-                *reinterpret_cast<float4 *>(x_out + (size_t)rs * K + 8 * i) = make_float4(x[0], x[1], x[2], x[3]);
-                *reinterpret_cast<float4 *>(x_out + (size_t)rs * K + 8 * i + 4) = make_float4(x[4], x[5], x[6], x[7]);
-            }
+            for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
         }
         const float total = block_sum(ss, red);
         rms = 1.0f / sqrtf(total / (float)K + eps);  // llama_run:79-116
     }
-    const size_t row_bytes = K / 2, row_scales = K / 32;
-    for (uint32_t base = threadIdx.x - lane; base < nw; base += kThreads) {
-        const uint32_t i = base + lane;
-        const bool valid = i < nw;  // whole 32-blocks are valid together (nw % 4 == 0)
-        float x[8];
-        if (valid) {
-            load8<SRC>(x, i, rs, K, src, erow);
-            if (SRC == SRC_EMBED || SRC == SRC_NORM) {
-                const float4 w0 = __ldg(reinterpret_cast<const float4 *>(norm_w + 8 * i));
-                const float4 w1 = __ldg(reinterpret_cast<const float4 *>(norm_w + 8 * i + 4));
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) x[j] = x[j] * rms * wv[j];
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) x[j] = 0.0f;
+    const bool valid = i < nw;  // whole 32-blocks are valid together (nw % 4 == 0)
+    float x[8];
+    if (valid) {
+        load8<SRC>(x, i, rs, K, src, erow);
+        if (SRC == SRC_EMBED) {
+            *reinterpret_cast<float4 *>(x_out + (size_t)rs * K + 8 * i) = make_float4(x[0], x[1], x[2], x[3]);
+            *reinterpret_cast<float4 *>(x_out + (size_t)rs * K + 8 * i + 4) = make_float4(x[4], x[5], x[6], x[7]);
         }
-        uint32_t words[8];
-        const int e1 = ptc::term_words8(x, words);
-        if (!valid) continue;
+        if (SRC == SRC_SWIGLU) {
+            float4 *g = reinterpret_cast<float4 *>(const_cast<float *>(src) + (size_t)rs * 2 * K + 16 * i);
 #pragma unroll
-        for (uint32_t t = 0; t < kTerms; ++t) {
-            const size_t tr = (size_t)r * kTerms + t;
-            *reinterpret_cast<uint32_t *>(act + tr * row_bytes + 4 * i) = words[t];
-            if ((i & 3) == 0) act_s[tr * row_scales + i / 4] = (uint8_t)(ptc::term_exp(e1, (int)t) + 127);
+            for (int e = 0; e < 4; ++e) g[e] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
+        if (SRC == SRC_EMBED || SRC == SRC_NORM) {
+            const float4 w0 = __ldg(reinterpret_cast<const float4 *>(norm_w + 8 * i));
+            const float4 w1 = __ldg(reinterpret_cast<const float4 *>(norm_w + 8 * i + 4));
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = x[e] * rms * wv[e];
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = 0.0f;
     }
-    if (SRC == SRC_SWIGLU) {
-        __syncthreads();
-        float4 *g = reinterpret_cast<float4 *>(const_cast<float *>(src) + (size_t)rs * 2 * K);
-        for (uint32_t i = threadIdx.x; i < K / 2; i += kThreads) g[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    uint32_t words[8];
+    const int e1 = ptc::term_words8(x, words);  // every lane of the warp takes part
+    if (!valid) return;
+    const size_t row_bytes = K / 2, row_scales = K / 32;
+#pragma unroll
+    for (uint32_t t = 0; t < kMaxTerms; ++t) {
+        if (t >= terms) break;
+        const size_t tr = (size_t)r * terms + t;
+        *reinterpret_cast<uint32_t *>(act + tr * row_bytes + 4 * i) = words[t];
+        if ((i & 3) == 0) act_s[tr * row_scales + i / 4] = (uint8_t)(ptc::term_exp(e1, (int)t) + 127);
     }
 }
 
 // RoPE of the q and k storage rows (rope-paired 16-row tiles: rows 0..7 = dims
 // j..j+7, rows 8..15 = dims j+half..), q to q_out in head-major order, k and v
-// to the bf16 cache of the row at its position; then the row's QKV sums are
-// cleared for the next layer.
+// to the bf16 cache of the row at its position; every value read is cleared for
+// the next layer's sums.  CTA (r, c): items c, c + gridDim.y, ... of row r
+// (item = a rope pair of q/k rows or one v row).
 __global__ void __launch_bounds__(kThreads) rows_rope_append_kernel(uint32_t qd, uint32_t kvd, uint32_t hd,
                                                                     float *qkv, float *q_out, uint16_t *kc,
                                                                     uint16_t *vc, const uint32_t *pos,
                                                                     const uint32_t *cache, uint32_t max_seq,
                                                                     const float *cos_t, const float *sin_t) {
-    const uint32_t r = blockIdx.x, half = hd / 2, n = qd + 2 * kvd;
+    const uint32_t r = blockIdx.x, half = hd / 2, n = qd + 2 * kvd, pairs = (qd + kvd) / 2;
     const uint32_t p = pos[r];
     const size_t c = cache ? cache[r] : r;
     float *row = qkv + (size_t)r * n;
-    if (p < max_seq) {
-        uint16_t *kdst = kc + (c * max_seq + p) * kvd, *vdst = vc + (c * max_seq + p) * kvd;
-        for (uint32_t i = threadIdx.x; i < (qd + kvd) / 2; i += kThreads) {
-            const uint32_t tile = i / 8, w = i % 8;
+    const bool in_cache = p < max_seq;
+    uint16_t *kdst = kc + (c * max_seq + (in_cache ? p : 0)) * kvd, *vdst = vc + (c * max_seq + (in_cache ? p : 0)) * kvd;
+    for (uint32_t it = blockIdx.y * kThreads + threadIdx.x; it < pairs + kvd; it += gridDim.y * kThreads) {
+        if (it < pairs) {
+            const uint32_t tile = it / 8, w = it % 8;
             const uint32_t s0 = tile * 16 + w;  // partner at s0 + 8
             const bool is_q = s0 < qd;
             const uint32_t lr = is_q ? s0 : s0 - qd;
             const uint32_t head = lr / hd, j = ((lr % hd) / 16) * 8 + w;
-            const float cs = cos_t[(size_t)p * half + j], sn = sin_t[(size_t)p * half + j];
             const float x0 = __ldcg(row + s0), x1 = __ldcg(row + s0 + 8);
+            row[s0] = 0.0f, row[s0 + 8] = 0.0f;
+            if (!in_cache) continue;
+            const float cs = cos_t[(size_t)p * half + j], sn = sin_t[(size_t)p * half + j];
             const float o0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));  // llama_run:135-136
             const float o1 = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
             if (is_q) {
@@ -208,11 +215,13 @@ __global__ void __launch_bounds__(kThreads) rows_rope_append_kernel(uint32_t qd,
                 kdst[head * hd + j] = f32_to_bf16_bits(o0);
                 kdst[head * hd + j + half] = f32_to_bf16_bits(o1);
             }
+        } else {
+            const uint32_t v = it - pairs;
+            const float x = __ldcg(row + qd + kvd + v);
+            row[qd + kvd + v] = 0.0f;
+            if (in_cache) vdst[v] = f32_to_bf16_bits(x);
         }
-        for (uint32_t i = threadIdx.x; i < kvd; i += kThreads) vdst[i] = f32_to_bf16_bits(__ldcg(row + qd + kvd + i));
     }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < n; i += kThreads) row[i] = 0.0f;
 }
 
 __device__ __forceinline__ void argmax_merge(float &bv, uint32_t &bi, float ov, uint32_t oi) {
@@ -285,24 +294,38 @@ int alloc(fp4x_llama_batch *b, T **p, size_t count) {
     return FP4X_OK;
 }
 
-// Term rows = 8 x R; out[R][n] += (or =) the sums.
-int linear(cudaStream_t st, uint32_t R, const QMat &w, const uint8_t *act, const uint8_t *act_s, float *out,
-           bool accumulate) {
-    const uint32_t m = R * kTerms;
+// Term rows = terms x R; out[R][n] = (or +=) the sums.
+int linear(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const QMat &w, float *out, bool accumulate) {
+    const uint32_t m = R * b->terms;
     const mma::Plan p = mma::plan(m, w.n, w.k);
-    mma::Mode mode = mma::OUT_RED_F32;
-    if (!accumulate) {
-        if (p.splits == 1) mode = mma::OUT_F32;
-        else if (cudaMemsetAsync(out, 0, (size_t)R * w.n * sizeof(float), st) != cudaSuccess)
-            return check_launch("llama_batch: clear");
+    if (mma::partials_bytes(p, m, w.n, b->terms) > b->mma_part_bytes) {
+        set_error("llama_batch: GEMM workspace too small");
+        return FP4X_EINVAL;
     }
-    return mma::launch(st, m, w.n, w.k, act, act_s, w.w, w.s, out, mode, p, kTerms);
+    return mma::launch(st, m, w.n, w.k, b->act, b->act_s, w.w, w.s, out, accumulate ? mma::OUT_ADD_F32 : mma::OUT_F32,
+                       p, b->terms, b->mma_part);
+}
+
+// Largest split-K scratch a pass of up to `rows` rows needs over the model's linears.
+size_t mma_ws_need(const fp4x_llama_model *m, uint32_t rows, uint32_t terms) {
+    size_t part = 0;
+    auto upd = [&](const QMat &w) {
+        for (uint32_t r = 1; r <= rows; ++r) {
+            const mma::Plan p = mma::plan(r * terms, w.n, w.k);
+            part = std::max(part, mma::partials_bytes(p, r * terms, w.n, terms));
+        }
+    };
+    const LayerW &L = m->layers[0];
+    upd(L.qkv), upd(L.o), upd(L.gu), upd(L.down), upd(m->lm_head);
+    return part;
 }
 
 template <int SRC>
-int decompose(cudaStream_t st, uint32_t R, uint32_t K, const float *src, float *x_out, const uint16_t *embed,
-              const uint32_t *tok, const float *norm_w, float eps, uint8_t *act, uint8_t *act_s, uint32_t row0 = 0) {
-    rows_decompose_kernel<SRC><<<R, kThreads, 0, st>>>(K, src, x_out, embed, tok, norm_w, eps, act, act_s, row0);
+int decompose(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, uint32_t K, const float *src, float *x_out,
+              const uint32_t *tok, const float *norm_w, uint32_t row0 = 0) {
+    const uint32_t chunks = (K / 8 + kThreads - 1) / kThreads;
+    rows_decompose_kernel<SRC><<<dim3(R, chunks), kThreads, 0, st>>>(K, src, x_out, b->m->embed, tok, norm_w,
+                                                                      b->m->lc.eps, b->act, b->act_s, row0, b->terms);
     return check_launch("llama_batch: decompose");
 }
 
@@ -340,31 +363,26 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
         LayerW &L = m->layers[l];
         uint16_t *kc = kbase + l * layer_kv, *vc = vbase + l * layer_kv;
         if (l == 0)
-            FP4X_TRY(decompose<SRC_EMBED>(st, R, c.dim, nullptr, b->x, m->embed, tok, L.attn_norm, c.eps, b->act,
-                                          b->act_s));
+            FP4X_TRY(decompose<SRC_EMBED>(b, st, R, c.dim, nullptr, b->x, tok, L.attn_norm));
         else
-            FP4X_TRY(decompose<SRC_NORM>(st, R, c.dim, b->x, nullptr, nullptr, nullptr, L.attn_norm, c.eps, b->act,
-                                         b->act_s));
-        FP4X_TRY(linear(st, R, L.qkv, b->act, b->act_s, b->qkv, true));
-        rows_rope_append_kernel<<<R, kThreads, 0, st>>>(qd, kvd, hd, b->qkv, b->q, kc, vc, pos, cache, b->max_seq,
+            FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.attn_norm));
+        FP4X_TRY(linear(b, st, R, L.qkv, b->qkv, false));
+        rows_rope_append_kernel<<<dim3(R, (qd + 3 * kvd + 2 * kThreads - 1) / (2 * kThreads)), kThreads, 0, st>>>(qd, kvd, hd, b->qkv, b->q, kc, vc, pos, cache, b->max_seq,
                                                         m->cos_t, m->sin_t);
         FP4X_TRY(check_launch("llama_batch: rope"));
         ap.kc = kc, ap.vc = vc;
         FP4X_TRY(attn::launch_engine(st, ap, hd, false));
-        FP4X_TRY(decompose<SRC_PLAIN>(st, R, qd, b->att, nullptr, nullptr, nullptr, nullptr, 0.0f, b->act, b->act_s));
-        FP4X_TRY(linear(st, R, L.o, b->act, b->act_s, b->x, true));
-        FP4X_TRY(decompose<SRC_NORM>(st, R, c.dim, b->x, nullptr, nullptr, nullptr, L.ffn_norm, c.eps, b->act,
-                                     b->act_s));
-        FP4X_TRY(linear(st, R, L.gu, b->act, b->act_s, b->gu, true));
-        FP4X_TRY(decompose<SRC_SWIGLU>(st, R, c.ffn, b->gu, nullptr, nullptr, nullptr, nullptr, 0.0f, b->act,
-                                       b->act_s));
-        FP4X_TRY(linear(st, R, L.down, b->act, b->act_s, b->x, true));
+        FP4X_TRY(decompose<SRC_PLAIN>(b, st, R, qd, b->att, nullptr, nullptr, nullptr));
+        FP4X_TRY(linear(b, st, R, L.o, b->x, true));
+        FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.ffn_norm));
+        FP4X_TRY(linear(b, st, R, L.gu, b->gu, false));
+        FP4X_TRY(decompose<SRC_SWIGLU>(b, st, R, c.ffn, b->gu, nullptr, nullptr, nullptr));
+        FP4X_TRY(linear(b, st, R, L.down, b->x, true));
     }
     const uint32_t RL = R - lm0;
     if (RL == 0) return FP4X_OK;  // no logits wanted (a prompt chunk before the last)
-    FP4X_TRY(decompose<SRC_NORM>(st, RL, c.dim, b->x, nullptr, nullptr, nullptr, m->final_norm, c.eps, b->act,
-                                 b->act_s, lm0));
-    FP4X_TRY(linear(st, RL, m->lm_head, b->act, b->act_s, b->logits, false));
+    FP4X_TRY(decompose<SRC_NORM>(b, st, RL, c.dim, b->x, nullptr, nullptr, m->final_norm, lm0));
+    FP4X_TRY(linear(b, st, RL, m->lm_head, b->logits, false));
     b->last_rows = RL;
     return FP4X_OK;
 }
@@ -417,6 +435,7 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     fp4x_llama_batch *b = new (std::nothrow) fp4x_llama_batch();
     if (!b) return FP4X_ENOMEM;
     b->m = m, b->rows = rows, b->max_seq = c.max_seq;
+    if (const char *e = getenv("FP4X_BATCH_TERMS")) b->terms = atoi(e) == 8 ? 8 : 4;
     b->len.assign(rows, 0);
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     const uint32_t kmax = std::max(std::max(c.dim, c.ffn), qd);
@@ -438,8 +457,10 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     if (!rc) rc = batch::alloc(b, &b->gu, (size_t)rows * 2 * c.ffn);
     if (!rc) rc = batch::alloc(b, &b->logits, (size_t)rows * c.vocab);
     if (!rc) rc = batch::alloc(b, &b->attn_ws, std::max<size_t>(16, b->attn_ws_bytes / 4));
-    if (!rc) rc = batch::alloc(b, &b->act, (size_t)rows * batch::kTerms * kmax / 2);
-    if (!rc) rc = batch::alloc(b, &b->act_s, (size_t)rows * batch::kTerms * kmax / 32);
+    if (!rc) rc = batch::alloc(b, &b->act, (size_t)rows * b->terms * kmax / 2);
+    if (!rc) rc = batch::alloc(b, &b->act_s, (size_t)rows * b->terms * kmax / 32);
+    b->mma_part_bytes = batch::mma_ws_need(m, rows, b->terms);
+    if (!rc) rc = batch::alloc(b, &b->mma_part, std::max<size_t>(4, b->mma_part_bytes / 4));
     if (!rc) rc = batch::alloc(b, &b->dec_tok, rows);
     if (!rc) rc = batch::alloc(b, &b->dec_pos, rows);
     if (!rc) rc = batch::alloc(b, &b->pf_tok, rows);

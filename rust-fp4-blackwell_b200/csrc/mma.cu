@@ -59,7 +59,9 @@ constexpr uint32_t kMaxStages = 8;
 constexpr uint32_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kBarBytes = 256;
 
-enum Mode : uint32_t { OUT_BF16 = 0, OUT_F32 = 1, OUT_RED_F32 = 2 };
+// Final write of an output element: bf16 store, f32 store, or f32 add into the
+// destination (a residual; one writer per element, so a plain load + store).
+enum Mode : uint32_t { OUT_BF16 = 0, OUT_F32 = 1, OUT_ADD_F32 = 2 };
 
 struct Geo {
     uint32_t nt, stages, sfb_atoms, stage_bytes, b_off, sfa_off, sfb_off, tmem_cols, sfa_col0, sfb_col0, smem;
@@ -90,8 +92,79 @@ struct Args {
     const uint8_t *sa, *sw;     // scales [m][k/32], [n][k/32]
     void *d;                    // [m / terms][n] bf16 or f32
     uint32_t mode;
-    uint32_t terms;             // 1, or 8: A rows 8t..8t+7 are the MXFP4 terms of token t (summed)
+    uint32_t terms;             // 1, 4 or 8: A rows T t .. T t + T - 1 are the MXFP4 terms of token t (summed)
+    uint32_t splits;            // K splits (blockIdx.z); > 1: partial sums to ws, added by splitk_reduce_kernel
+    float *ws;                  // [splits][m / terms][n] partial sums
 };
+
+__device__ __forceinline__ void emit(const Args &a, uint32_t tok, uint32_t row, float v) {
+    const size_t o = (size_t)tok * a.n + row;
+    if (a.mode == OUT_BF16)
+        reinterpret_cast<uint16_t *>(a.d)[o] = f32_to_bf16_bits(v);
+    else if (a.mode == OUT_F32)
+        reinterpret_cast<float *>(a.d)[o] = v;
+    else
+        reinterpret_cast<float *>(a.d)[o] += v;
+}
+
+// Split-K: out[t][r] (final write of `mode`) = sum over splits, in split order.
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, uint32_t splits, uint32_t tokens, uint32_t n,
+                                     void *d, uint32_t mode) {
+    const size_t total = (size_t)tokens * n, stride = (size_t)gridDim.x * blockDim.x;
+    Args a{};
+    a.n = n, a.d = d, a.mode = mode;
+    if ((n & 3u) == 0) {
+        const size_t q = total / 4;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < q; i += stride) {
+            float4 acc = __ldcg(reinterpret_cast<const float4 *>(ws) + i);
+            for (uint32_t sp = 1; sp < splits; ++sp) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(ws + sp * total) + i);
+                acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+            }
+            const uint32_t tk = (uint32_t)(4 * i / n), r = (uint32_t)(4 * i % n);
+            emit(a, tk, r, acc.x), emit(a, tk, r + 1, acc.y), emit(a, tk, r + 2, acc.z), emit(a, tk, r + 3, acc.w);
+        }
+        return;
+    }
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        float acc = __ldcg(ws + i);
+        for (uint32_t sp = 1; sp < splits; ++sp) acc += __ldcg(ws + sp * total + i);
+        emit(a, (uint32_t)(i / n), (uint32_t)(i % n), acc);
+    }
+}
+
+// Accumulator -> outputs for the 128 epilogue threads (thread = weight row
+// row0 + 32q + lane; TMEM lane quarter q).  Column c of the tile is A row tok0 + c;
+// T consecutive columns are the terms of one token and are added.  With split K
+// the sums go to this split's partial slice.
+template <uint32_t T>
+__device__ void epilogue_sums(const Args &a, uint32_t tbase, uint32_t q, uint32_t row, uint32_t tok0) {
+    const bool row_ok = row < a.n;
+    const uint32_t tokens = a.m / T;
+    for (uint32_t c0 = 0; c0 < a.nt; c0 += 32) {
+        float v[4][8];
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u)
+            if (c0 + 8 * u < a.nt) tc::tmem_ld_x8(tbase + ((32 * q) << 16) + c0 + 8 * u, v[u]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u) {
+            if (c0 + 8 * u >= a.nt) continue;
+#pragma unroll
+            for (uint32_t j = 0; j < 8; j += T) {
+                float sum = v[u][j];
+#pragma unroll
+                for (uint32_t e = 1; e < T; ++e) sum += v[u][j + e];
+                const uint32_t tk = (tok0 + c0 + 8 * u + j) / T;
+                if (!row_ok || tk >= tokens) continue;
+                if (a.splits > 1)
+                    a.ws[((size_t)blockIdx.z * tokens + tk) * a.n + row] = sum;
+                else
+                    emit(a, tk, row, sum);
+            }
+        }
+    }
+}
 
 // Bounded wait that also gives up when another role of the CTA has aborted.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
@@ -206,62 +279,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         const uint32_t t = threadIdx.x - 64;  // 0..127
+        // The scale bytes of stage i are loaded kScaleAhead stages early (a register
+        // ring shifted every stage), so the global-load latency overlaps the MMAs
+        // of the stages in between instead of adding to every stage.
+        constexpr uint32_t kScaleAhead = 4;
+        uint2 rw[kScaleAhead], rb0[kScaleAhead], rb1[kScaleAhead];
+        auto fetch = [&](uint32_t i, uint2 &w, uint2 &b0, uint2 &b1) {
+            w = b0 = b1 = make_uint2(0, 0);
+            if (i >= nst) return;
+            const uint32_t kb0 = (s0 + i) * 8;
+            w = load_scales8(a.sw, row0 + t, a.n, kb0, kbt);
+            if (t < a.nt) b0 = load_scales8(a.sa, tok0 + t, a.m, kb0, kbt);
+            if (G.sfb_atoms > 1 && t + 128 < a.nt) b1 = load_scales8(a.sa, tok0 + t + 128, a.m, kb0, kbt);
+        };
+#pragma unroll
+        for (uint32_t j = 0; j < kScaleAhead; ++j) fetch(j, rw[j], rb0[j], rb1[j]);
         for (uint32_t i = 0; i < nst; ++i) {
             const uint32_t slot = i % S;
             if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
             uint8_t *st = smem + slot * G.stage_bytes;
-            const uint32_t kb0 = (s0 + i) * 8;
-            const uint2 wa = load_scales8(a.sw, row0 + t, a.n, kb0, kbt);
-            *reinterpret_cast<uint32_t *>(st + G.sfa_off + tc::scale_atom_off(t, 0)) = wa.x;
-            *reinterpret_cast<uint32_t *>(st + G.sfa_off + 512 + tc::scale_atom_off(t, 0)) = wa.y;
-            for (uint32_t q = 0; q < G.sfb_atoms; ++q) {
-                const uint32_t r = t + 128 * q;
-                const uint2 wb = r < a.nt ? load_scales8(a.sa, tok0 + r, a.m, kb0, kbt) : make_uint2(0, 0);
-                *reinterpret_cast<uint32_t *>(st + G.sfb_off + (q * 2) * 512 + tc::scale_atom_off(t, 0)) = wb.x;
-                *reinterpret_cast<uint32_t *>(st + G.sfb_off + (q * 2 + 1) * 512 + tc::scale_atom_off(t, 0)) = wb.y;
+            const uint32_t off = tc::scale_atom_off(t, 0);
+            *reinterpret_cast<uint32_t *>(st + G.sfa_off + off) = rw[0].x;
+            *reinterpret_cast<uint32_t *>(st + G.sfa_off + 512 + off) = rw[0].y;
+            *reinterpret_cast<uint32_t *>(st + G.sfb_off + off) = rb0[0].x;
+            *reinterpret_cast<uint32_t *>(st + G.sfb_off + 512 + off) = rb0[0].y;
+            if (G.sfb_atoms > 1) {
+                *reinterpret_cast<uint32_t *>(st + G.sfb_off + 1024 + off) = rb1[0].x;
+                *reinterpret_cast<uint32_t *>(st + G.sfb_off + 1536 + off) = rb1[0].y;
             }
             fence_proxy_async_smem();
             mbar_arrive(&full_s[slot]);
+#pragma unroll
+            for (uint32_t j = 0; j + 1 < kScaleAhead; ++j) rw[j] = rw[j + 1], rb0[j] = rb0[j + 1], rb1[j] = rb1[j + 1];
+            fetch(i + kScaleAhead, rw[kScaleAhead - 1], rb0[kScaleAhead - 1], rb1[kScaleAhead - 1]);
         }
         // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31
         bool ok = wait_or_abort(accb, 0, abort);
         ok = __all_sync(0xffffffffu, ok);
         tc::fence_after_sync();
+        const uint32_t q = (uint32_t)warp & 3, row = row0 + 32 * q + lane;
         if (ok) {
-            const uint32_t q = (uint32_t)warp & 3, row = row0 + 32 * q + lane;
-            const bool row_ok = row < a.n;
-            for (uint32_t c0 = 0; c0 < a.nt; c0 += 8) {
-                float v[8];
-                tc::tmem_ld_x8(tbase + ((32 * q) << 16) + c0, v);
-                tc::tmem_wait_ld();
-                if (a.terms == 8) {  // the 8 columns are the terms of one token: add them
-                    const uint32_t tok = (tok0 + c0) >> 3;
-                    if (!row_ok || 8 * tok >= a.m) continue;
-                    float sum = v[0];
-#pragma unroll
-                    for (uint32_t j = 1; j < 8; ++j) sum += v[j];
-                    const size_t o = (size_t)tok * a.n + row;
-                    if (a.mode == OUT_BF16)
-                        reinterpret_cast<uint16_t *>(a.d)[o] = f32_to_bf16_bits(sum);
-                    else if (a.mode == OUT_F32)
-                        reinterpret_cast<float *>(a.d)[o] = sum;
-                    else
-                        atomicAdd(reinterpret_cast<float *>(a.d) + o, sum);
-                    continue;
-                }
-#pragma unroll
-                for (uint32_t j = 0; j < 8; ++j) {
-                    const uint32_t tok = tok0 + c0 + j;
-                    if (!row_ok || tok >= a.m) continue;
-                    const size_t o = (size_t)tok * a.n + row;
-                    if (a.mode == OUT_BF16)
-                        reinterpret_cast<uint16_t *>(a.d)[o] = f32_to_bf16_bits(v[j]);
-                    else if (a.mode == OUT_F32)
-                        reinterpret_cast<float *>(a.d)[o] = v[j];
-                    else
-                        atomicAdd(reinterpret_cast<float *>(a.d) + o, v[j]);
-                }
-            }
+            if (a.terms == 8) epilogue_sums<8>(a, tbase, q, row, tok0);
+            else if (a.terms == 4) epilogue_sums<4>(a, tbase, q, row, tok0);
+            else epilogue_sums<1>(a, tbase, q, row, tok0);
         }
     }
     tc::fence_before_sync();
@@ -270,11 +330,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tbase, G.tmem_cols);
     }
-}
-
-__global__ void f32_to_bf16_kernel(const float *__restrict__ x, uint16_t *__restrict__ y, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        y[i] = f32_to_bf16_bits(x[i]);
 }
 
 // Known-answer kernel of the reference's fp4_mma_allones: A = B = 0x22 bytes
@@ -344,15 +399,22 @@ struct Plan {
     Geo g;
 };
 
-inline Plan plan(uint32_t m, uint32_t n, uint32_t k) {
+inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true) {
     Plan p;
     p.nt = m >= 256 ? 256 : (m + 7) / 8 * 8;
     p.m_tiles = (m + p.nt - 1) / p.nt;
     p.n_tiles = (n + 127) / 128;
     p.kst = (k + kStageK - 1) / kStageK;
     const uint32_t tiles = p.m_tiles * p.n_tiles, sms = (uint32_t)num_sms();
-    uint32_t splits = 1;
-    if (tiles < sms) splits = std::min(p.kst, (sms + tiles - 1) / tiles);
+    // One CTA per SM: time ~ waves x (stages per CTA + ~2 stages of pipeline fill
+    // and epilogue).  Take the fewest splits that reach the minimum (each split
+    // adds an fp32 partial per output).
+    uint32_t splits = 1, best = ~0u;
+    for (uint32_t s = 1; s <= (allow_split ? std::min(p.kst, 16u) : 1u); ++s) {
+        const uint32_t waves = (tiles * s + sms - 1) / sms, per = (p.kst + s - 1) / s;
+        const uint32_t cost = waves * (per + 2) + (s > 1 ? 2 : 0);
+        if (cost < best) best = cost, splits = s;
+    }
     p.kps = (p.kst + splits - 1) / splits;
     p.splits = (p.kst + p.kps - 1) / p.kps;
     p.g = geometry(p.nt);
@@ -369,8 +431,14 @@ int validate(uint32_t m, uint32_t n, uint32_t k, const void *a, const void *sa, 
     return FP4X_OK;
 }
 
+// Split-K scratch: partials [splits][m / terms][n] f32.
+inline size_t partials_bytes(const Plan &p, uint32_t m, uint32_t n, uint32_t terms) {
+    return p.splits > 1 ? (size_t)p.splits * (m / terms) * n * sizeof(float) : 0;
+}
+
+// partials: split-K scratch of partials_bytes() (unused when p.splits == 1).
 int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa,
-           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms = 1) {
+           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms, float *partials) {
     CUtensorMap map_w, map_a;
     if (!tc::make_map_sw128(&map_w, w, k / 2, n, 128) || !tc::make_map_sw128(&map_a, a, k / 2, m, p.nt)) {
         set_error("fp4_mma: cuTensorMapEncodeTiled failed (m=%u n=%u k=%u)", m, n, k);
@@ -386,8 +454,17 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
         set_error("fp4_mma: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
         return FP4X_ECUDA;
     }
-    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms};
+    if (p.splits > 1 && !partials) {
+        set_error("fp4_mma: split-K launch without a workspace");
+        return FP4X_EINVAL;
+    }
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials};
     mxf4_gemm_kernel<<<dim3(p.m_tiles, p.n_tiles, p.splits), kThreads, p.g.smem, s>>>(map_w, map_a, args);
+    if (p.splits > 1) {
+        const size_t total = (size_t)(m / terms) * n;
+        const uint32_t blocks = (uint32_t)std::min<size_t>((total / 4 + 255) / 256 + 1, 8u * (uint32_t)num_sms());
+        splitk_reduce_kernel<<<blocks, 256, 0, s>>>(partials, p.splits, m / terms, n, d, (uint32_t)mode);
+    }
     return check_launch("fp4_mma");
 }
 
@@ -398,8 +475,7 @@ using namespace fp4x;
 
 extern "C" size_t fp4_mma_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
     if (m == 0 || n == 0 || k == 0) return 0;
-    const mma::Plan p = mma::plan(m, n, k);
-    return p.splits > 1 ? (size_t)m * n * sizeof(float) : 0;
+    return mma::partials_bytes(mma::plan(m, n, k), m, n, 1);
 }
 
 extern "C" int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
@@ -408,26 +484,20 @@ extern "C" int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k,
     if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d_bf16)) return e;
     const mma::Plan p = mma::plan(m, n, k);
     cudaStream_t s = (cudaStream_t)stream;
-    if (p.splits == 1) return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d_bf16, mma::OUT_BF16, p);
-    const size_t need = (size_t)m * n * sizeof(float);
-    FP4X_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
-                 "fp4_mma: split-K needs a 16-byte aligned workspace of %zu bytes (fp4_mma_workspace_size)", need);
-    if (cudaMemsetAsync(workspace, 0, need, s) != cudaSuccess) return check_launch("fp4_mma workspace clear");
-    if (int e = mma::launch(s, m, n, k, a, a_scales, w, w_scales, workspace, mma::OUT_RED_F32, p)) return e;
-    const size_t total = (size_t)m * n;
-    const int blocks = (int)std::min<size_t>((total + 255) / 256, 4 * (size_t)num_sms());
-    mma::f32_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float *>(workspace), d_bf16, total);
-    return check_launch("fp4_mma convert");
+    const size_t need = mma::partials_bytes(p, m, n, 1);
+    if (p.splits > 1)
+        FP4X_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+                     "fp4_mma: split-K needs a 16-byte aligned workspace of %zu bytes (fp4_mma_workspace_size)", need);
+    return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d_bf16, mma::OUT_BF16, p, 1,
+                       static_cast<float *>(workspace));
 }
 
+// fp32 output without a workspace: one CTA per output tile over the whole K.
 extern "C" int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
                            const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float *d) {
     if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d)) return e;
-    const mma::Plan p = mma::plan(m, n, k);
-    cudaStream_t s = (cudaStream_t)stream;
-    if (p.splits == 1) return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p);
-    if (cudaMemsetAsync(d, 0, (size_t)m * n * sizeof(float), s) != cudaSuccess) return check_launch("fp4_mma_f32 clear");
-    return mma::launch(s, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_RED_F32, p);
+    const mma::Plan p = mma::plan(m, n, k, false);
+    return mma::launch((cudaStream_t)stream, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p, 1, nullptr);
 }
 
 extern "C" int fp4_mma_allones(fp4x_stream_t stream, float *out) {
