@@ -208,6 +208,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / 32;
     const uint32_t s0 = blockIdx.z * a.kps, s1 = min(kst, s0 + a.kps);
     const uint32_t nst = s1 > s0 ? s1 - s0 : 0;
+    // CTAs walk their K stages in rotated order (start = weight tile index mod
+    // stages) so that concurrent CTAs do not all read the same activation lines
+    // of L2 at the same moment.
+    const uint32_t rot = nst ? blockIdx.y % nst : 0;
+    auto stage_of = [&](uint32_t i) { return s0 + (i + rot < nst ? i + rot : i + rot - nst); };
 
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < S; ++i) {
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
                 uint8_t *st = smem + slot * G.stage_bytes;
                 mbar_arrive_expect_tx(&full_t[slot], kTileA + a.nt * 128);
-                const int32_t kx = (int32_t)((s0 + i) * 128);
+                const int32_t kx = (int32_t)(stage_of(i) * 128);
                 tc::tma_load_2d(st, &map_w, kx, (int32_t)row0, &full_t[slot]);
                 tc::tma_load_2d(st + G.b_off, &map_a, kx, (int32_t)tok0, &full_t[slot]);
                 issued = i + 1;
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto fetch = [&](uint32_t i, uint2 &w, uint2 &b0, uint2 &b1) {
             w = b0 = b1 = make_uint2(0, 0);
             if (i >= nst) return;
-            const uint32_t kb0 = (s0 + i) * 8;
+            const uint32_t kb0 = stage_of(i) * 8;
             w = load_scales8(a.sw, row0 + t, a.n, kb0, kbt);
             if (t < a.nt) b0 = load_scales8(a.sa, tok0 + t, a.m, kb0, kbt);
             if (G.sfb_atoms > 1 && t + 128 < a.nt) b1 = load_scales8(a.sa, tok0 + t + 128, a.m, kb0, kbt);
