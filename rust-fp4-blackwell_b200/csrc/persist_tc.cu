@@ -945,9 +945,28 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     CST(16);
     if (!c.ok) return;
     const uint32_t mt = p.dim / 128;
-    for (uint32_t t = warp >> 2; t < mt; t += kCW / 4) {
-        const float s = acc_row(c.tbase, 8 * t);
-        add_all_ranks(p.yr, p.tp_size, t * 128 + 32 * (warp & 3) + lane, s);
+    if (p.tp_size == 1) {
+        // The CTA's whole down partial (dim values) is added into Y by one bulk
+        // reduction: the L2 applies it a sector at a time instead of one element
+        // per red.add (148 CTAs x dim element updates per layer otherwise).  The
+        // staging buffer (the activation staging area, free once the down MMAs
+        // are done) is read by the bulk copy before this thread reaches the next
+        // grid barrier.
+        float *stg = reinterpret_cast<float *>(c.smem + c.L.xv);
+        for (uint32_t t = warp >> 2; t < mt; t += kCW / 4)
+            stg[t * 128 + 32 * (warp & 3) + lane] = acc_row(c.tbase, 8 * t);
+        fence_proxy_async_smem();
+        csync();
+        if (threadIdx.x == 0) {
+            tc::bulk_reduce_add_f32(p.Y, stg, p.dim * 4);
+            tc::bulk_commit();
+            tc::bulk_wait_all();
+        }
+    } else {
+        for (uint32_t t = warp >> 2; t < mt; t += kCW / 4) {
+            const float s = acc_row(c.tbase, 8 * t);
+            add_all_ranks(p.yr, p.tp_size, t * 128 + 32 * (warp & 3) + lane, s);
+        }
     }
     CST(17);
 }

@@ -136,5 +136,17 @@ __host__ __device__ constexpr uint32_t scale_atom_off(uint32_t r, uint32_t j) {
 // 128-byte x box_rows box and the 128-byte swizzle.  Returns false on failure.
 bool make_map_sw128(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows);
 
+// Bulk reduction of `bytes` (multiple of 16) of f32 from shared memory into global
+// memory (element-wise add, performed by the L2 a sector at a time), tracked by
+// the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_reduce_add_f32(float *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk operation of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 }  // namespace tc
 }  // namespace fp4x
