@@ -419,21 +419,30 @@ def run_batch(args):
     (prefill not timed); step = one token of every sequence; value = tokens of
     all sequences / device time.  Bytes per step = MXFP4 weights + the bf16 K/V
     rows every sequence reads (at the mean position of the timed steps)."""
+    import datetime
     import torch
-    from fp4x import engine
-    torch.cuda.set_device(0)
+    import torch.distributed as dist
+    from fp4x import engine, tp
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     base = engine.LLAMA3_8B if args.batch_model == "llama8b" else engine.TINYLLAMA
     B, ctx = args.batch, args.batch_ctx
     cfg = dict(base, max_seq=ctx + args.warmup + args.steps + 8)
-    m = engine.Model(cfg)
-    b = engine.Batch(m, B)
+    m = tp.create_model(cfg) if world > 1 else engine.Model(cfg)
+    b = tp.create_batch(m, B) if world > 1 else engine.Batch(m, B)
     for s in range(B):
         b.set_length(s, ctx, (17 + 31 * s) % cfg["vocab"])
     b.decode(args.warmup)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
+    with ClockSampler(local) as clk:
         if args.profile_region:
             torch.cuda.profiler.start()
         e0.record(st)
@@ -443,23 +452,32 @@ def run_batch(args):
         if args.profile_region:
             torch.cuda.profiler.stop()
     t = e0.elapsed_time(e1) * 1e-3
-    wbytes = m.weight_bytes()
-    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    wbytes = m.weight_bytes()  # this rank's shard
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"] // world
     mean_seq = ctx + args.warmup + (args.steps + 1) / 2
     kv_bytes = B * mean_seq * cfg["n_layers"] * kvd * 2 * 2
     per_step = t / args.steps
     peak, peak_kind = hbm_peak()
     b.close()
     m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
     line = {"metric": f"batched MXFP4 decode tok/s ({args.batch_model} shape, batch {B})", "value": B * args.steps / t,
-            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "mxf4 x mxf4(8-term) -> f32", "data": "synthetic (seeded N(0,0.02) weights -> MXFP4)",
             "config": {"workload": "config4-batch" if args.batch_model == "llama8b" else "tinyllama-batch",
-                       "batch": B, "context": ctx,
+                       "batch": B, "context": ctx, "tp": world,
                        "kv": "zero-filled cache of ctx positions per sequence (prefill not timed)",
                        "l2": "weights and KV caches far above L2 (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": "batched decode step (fp4_mma + attention)",
+            "roofline": {"bound": "hbm", "kernel": "batched decode step (fp4_mma + attention), rank 0 shard",
                          "achieved": (wbytes + kv_bytes) / per_step / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": (wbytes + kv_bytes) / per_step / 1e9 / peak,
                          "bytes_per_step": wbytes + kv_bytes, "weight_bytes": wbytes, "kv_bytes": kv_bytes,

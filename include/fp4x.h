@@ -275,8 +275,13 @@ FP4X_API size_t llama_model_weight_bytes(const fp4x_llama_model *m);
  * (llama_run/src/main.rs:544-587); here `rows` sequences with their own bf16 KV
  * caches ([layer][rows][max_seq][kvd]) run through the model's weights together,
  * every linear layer on the tcgen05 fp4_mma GEMM (activations as 8-term MXFP4
- * sums, fp32 accumulation).  Single GPU (tp_size 1).  The model handle must
- * outlive the batch. */
+ * sums, fp32 accumulation).  The model handle must outlive the batch.  Under
+ * tensor parallelism (a model created with tp_size > 1) every rank creates its
+ * batch over its shard, exchanges the 64-byte handles (llama_batch_tp_handle on
+ * every rank, gathered in rank order) and calls llama_batch_tp_connect; the
+ * row-parallel O and down outputs are then summed across ranks over NVLink peer
+ * memory and the argmax runs across the vocab shards.  All ranks must issue the
+ * same batch calls in the same order. */
 typedef struct fp4x_llama_batch fp4x_llama_batch;
 FP4X_API int llama_batch_create(fp4x_llama_model *m, uint32_t rows /* 1..256 */, fp4x_llama_batch **out);
 FP4X_API int llama_batch_destroy(fp4x_llama_batch *b);
@@ -299,6 +304,8 @@ FP4X_API int llama_batch_tokens(fp4x_llama_batch *b, uint32_t seq, uint32_t *out
 /* Logits of the last pass to a HOST array [*rows_out][vocab] (decode: one row
  * per sequence; prefill: the last prompt token).  Synchronous. */
 FP4X_API int llama_batch_logits(fp4x_llama_batch *b, float *logits_host, uint32_t *rows_out);
+FP4X_API int llama_batch_tp_handle(fp4x_llama_batch *b, void *handle_out /* 64 bytes */);
+FP4X_API int llama_batch_tp_connect(fp4x_llama_batch *b, const void *handles /* tp_size x 64 bytes */);
 /* Bytes of the batch's KV caches. */
 FP4X_API size_t llama_batch_kv_bytes(const fp4x_llama_batch *b);
 

@@ -63,6 +63,10 @@ struct fp4x_llama_batch {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     uint32_t last_rows = 0;  // logits rows of the last pass
+    // tensor parallelism: row-parallel O / down outputs [rows][dim] before the
+    // cross-rank allreduce, and the batch exchange area shared with the peers
+    float *part = nullptr;
+    fp4x::tp::RowExchange *rx = nullptr;
 };
 
 namespace fp4x {
@@ -373,11 +377,21 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
         ap.kc = kc, ap.vc = vc;
         FP4X_TRY(attn::launch_engine(st, ap, hd, false));
         FP4X_TRY(decompose<SRC_PLAIN>(b, st, R, qd, b->att, nullptr, nullptr, nullptr));
-        FP4X_TRY(linear(b, st, R, L.o, b->x, true));
+        if (b->rx) {  // row-parallel O: local partial, then the cross-rank sum into the residual
+            FP4X_TRY(linear(b, st, R, L.o, b->part, false));
+            FP4X_TRY(tp::rows_allreduce_add(st, b->rx, b->part, b->x, (size_t)R * c.dim));
+        } else {
+            FP4X_TRY(linear(b, st, R, L.o, b->x, true));
+        }
         FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.ffn_norm));
         FP4X_TRY(linear(b, st, R, L.gu, b->gu, false));
         FP4X_TRY(decompose<SRC_SWIGLU>(b, st, R, c.ffn, b->gu, nullptr, nullptr, nullptr));
-        FP4X_TRY(linear(b, st, R, L.down, b->x, true));
+        if (b->rx) {  // row-parallel down
+            FP4X_TRY(linear(b, st, R, L.down, b->part, false));
+            FP4X_TRY(tp::rows_allreduce_add(st, b->rx, b->part, b->x, (size_t)R * c.dim));
+        } else {
+            FP4X_TRY(linear(b, st, R, L.down, b->x, true));
+        }
     }
     const uint32_t RL = R - lm0;
     if (RL == 0) return FP4X_OK;  // no logits wanted (a prompt chunk before the last)
@@ -387,16 +401,23 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
     return FP4X_OK;
 }
 
+// Per-row argmax of the last pass's logits (across ranks under tensor parallelism).
+int argmax(fp4x_llama_batch *b, cudaStream_t st, uint32_t rows, uint32_t seq, uint32_t next_pos) {
+    fp4x_llama_model *m = b->m;
+    if (b->rx)
+        return tp::rows_argmax(st, b->rx, rows, m->lc.vocab, m->v0, b->logits, b->dec_tok, b->dec_pos, b->ids,
+                               b->max_seq, seq, next_pos);
+    rows_argmax_kernel<<<rows, 1024, 0, st>>>(m->lc.vocab, b->logits, b->dec_tok, b->dec_pos, b->ids, b->max_seq, seq,
+                                              next_pos);
+    return check_launch("llama_batch: argmax");
+}
+
 int build_graph(fp4x_llama_batch *b) {
     if (b->exec) return FP4X_OK;
     cudaStream_t st = b->cap_stream;
     FP4X_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     int rc = forward(b, st, b->rows, b->dec_tok, b->dec_pos, nullptr, 0);
-    if (!rc) {
-        rows_argmax_kernel<<<b->rows, 1024, 0, st>>>(b->m->lc.vocab, b->logits, b->dec_tok, b->dec_pos, b->ids,
-                                                      b->max_seq, ~0u, 0);
-        rc = check_launch("llama_batch: argmax");
-    }
+    if (!rc) rc = argmax(b, st, b->rows, ~0u, 0);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &g);
     if (rc) {
@@ -411,6 +432,7 @@ int build_graph(fp4x_llama_batch *b) {
 
 void destroy(fp4x_llama_batch *b) {
     if (!b) return;
+    tp::row_destroy(b->rx);
     if (b->exec) cudaGraphExecDestroy(b->exec);
     if (b->graph) cudaGraphDestroy(b->graph);
     if (b->cap_stream) cudaStreamDestroy(b->cap_stream);
@@ -426,8 +448,6 @@ using namespace fp4x;
 extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama_batch **out) {
     FP4X_REQUIRE(m && out, "llama_batch_create: null pointer");
     FP4X_REQUIRE(rows >= 1 && rows <= 256, "llama_batch_create: rows %u not in [1, 256]", rows);
-    FP4X_REQUIRE(m->cfg.tp_size <= 1, "llama_batch_create: the batched engine runs on one GPU (tp_size %u)",
-                 m->cfg.tp_size);
     const fp4x_llama_config &c = m->lc;
     FP4X_REQUIRE(c.dim % 64 == 0 && c.ffn % 64 == 0 && (c.n_heads * c.head_dim) % 64 == 0,
                  "llama_batch_create: dim, ffn and n_heads * head_dim must be multiples of 64");
@@ -468,6 +488,10 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     if (!rc) rc = batch::alloc(b, &b->pf_cache, rows);
     if (!rc) rc = batch::alloc(b, &b->prompt, c.max_seq);
     if (!rc) rc = batch::alloc(b, &b->ids, (size_t)rows * c.max_seq);
+    if (!rc && m->cfg.tp_size > 1) {
+        rc = batch::alloc(b, &b->part, (size_t)rows * c.dim);
+        if (!rc) rc = tp::row_create(&b->rx, m->cfg.tp_rank, m->cfg.tp_size, (size_t)rows * c.dim);
+    }
     if (!rc && (cudaMemset(b->qkv, 0, (size_t)rows * (qd + 2 * kvd) * 4) != cudaSuccess ||
                 cudaMemset(b->gu, 0, (size_t)rows * 2 * c.ffn * 4) != cudaSuccess ||
                 cudaMemset(b->dec_tok, 0, rows * 4) != cudaSuccess || cudaMemset(b->dec_pos, 0, rows * 4) != cudaSuccess ||
@@ -492,6 +516,7 @@ extern "C" int llama_batch_destroy(fp4x_llama_batch *b) {
 extern "C" int llama_batch_prefill(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t seq, const uint32_t *tokens,
                                    uint32_t n) {
     FP4X_REQUIRE(b && tokens, "llama_batch_prefill: null pointer");
+    FP4X_REQUIRE(!b->rx || b->rx->connected, "llama_batch_prefill: tensor-parallel batch not connected");
     FP4X_REQUIRE(seq < b->rows, "llama_batch_prefill: sequence %u of %u", seq, b->rows);
     FP4X_REQUIRE(n >= 1 && b->len[seq] + n < b->max_seq, "llama_batch_prefill: %u tokens after %u exceed max_seq %u",
                  n, b->len[seq], b->max_seq);
@@ -510,9 +535,7 @@ extern "C" int llama_batch_prefill(fp4x_llama_batch *b, fp4x_stream_t stream, ui
         const bool last = i0 + R == n;
         FP4X_TRY(batch::forward(b, st, R, b->pf_tok, b->pf_pos, b->pf_cache, last ? R - 1 : R));
         if (last) {
-            batch::rows_argmax_kernel<<<1, 1024, 0, st>>>(b->m->lc.vocab, b->logits, b->dec_tok, b->dec_pos, b->ids,
-                                                           b->max_seq, seq, pos0 + R);
-            FP4X_TRY(check_launch("llama_batch_prefill: argmax"));
+            FP4X_TRY(batch::argmax(b, st, 1, seq, pos0 + R));
         }
     }
     b->len[seq] += n;  // K/V of the prompt cached; the next token sits at position len
@@ -537,6 +560,7 @@ extern "C" int llama_batch_set_length(fp4x_llama_batch *b, fp4x_stream_t stream,
 
 extern "C" int llama_batch_decode(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t n_steps) {
     FP4X_REQUIRE(b, "llama_batch_decode: null pointer");
+    FP4X_REQUIRE(!b->rx || b->rx->connected, "llama_batch_decode: tensor-parallel batch not connected");
     for (uint32_t s = 0; s < b->rows; ++s)
         FP4X_REQUIRE(b->len[s] + n_steps < b->max_seq, "llama_batch_decode: sequence %u at %u + %u steps exceeds %u", s,
                      b->len[s], n_steps, b->max_seq);
@@ -575,4 +599,16 @@ extern "C" size_t llama_batch_kv_bytes(const fp4x_llama_batch *b) {
     if (!b) return 0;
     const fp4x_llama_config &c = b->m->lc;
     return (size_t)2 * c.n_layers * b->rows * b->max_seq * c.n_kv_heads * c.head_dim * 2;
+}
+
+extern "C" int llama_batch_tp_handle(fp4x_llama_batch *b, void *handle_out) {
+    FP4X_REQUIRE(b && handle_out, "llama_batch_tp_handle: null pointer");
+    FP4X_REQUIRE(b->rx, "llama_batch_tp_handle: the model is not tensor parallel");
+    return tp::row_export_handle(b->rx, handle_out);
+}
+
+extern "C" int llama_batch_tp_connect(fp4x_llama_batch *b, const void *handles) {
+    FP4X_REQUIRE(b && handles, "llama_batch_tp_connect: null pointer");
+    FP4X_REQUIRE(b->rx, "llama_batch_tp_connect: the model is not tensor parallel");
+    return tp::row_connect(b->rx, handles);
 }

@@ -55,6 +55,8 @@ SIGNATURES = {
     "llama_batch_tokens": (C.c_int, [C.c_void_p, C.c_uint32, _u32p, C.c_uint32, _u32p]),
     "llama_batch_logits": (C.c_int, [C.c_void_p, _f32p, _u32p]),
     "llama_batch_kv_bytes": (C.c_size_t, [C.c_void_p]),
+    "llama_batch_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "llama_batch_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
 }
 
 
@@ -235,3 +237,14 @@ class Batch:
 
     def kv_bytes(self) -> int:
         return int(self.L.llama_batch_kv_bytes(self._h))
+
+    def tp_handle(self) -> bytes:
+        """64-byte IPC handle of this rank's batch exchange area (tensor parallel)."""
+        buf = C.create_string_buffer(64)
+        check(self.L.llama_batch_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Map every rank's batch exchange area (handles in rank order)."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        check(self.L.llama_batch_tp_connect(self._h, blob))

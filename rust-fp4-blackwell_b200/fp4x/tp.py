@@ -40,3 +40,13 @@ def create_model(cfg: dict, group=None):
     if world > 1:
         m.tp_connect(exchange_handles(m.tp_handle(), group))
     return m
+
+
+def create_batch(model, rows: int, group=None):
+    """The batched engine over this rank's shard, connected to the other ranks."""
+    import torch.distributed as dist
+    from .engine import Batch
+    b = Batch(model, rows)
+    if dist.get_world_size(group) > 1:
+        b.tp_connect(exchange_handles(b.tp_handle(), group))
+    return b

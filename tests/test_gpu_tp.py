@@ -109,3 +109,55 @@ def test_tp2_matches_oracle(path):
     for r, out in res.items():
         assert out["logits_err"] <= 1e-2, (r, out)
         assert out["generate_equal"], (r, out)
+
+
+def _batch_worker(rank, world, port, cfg, result):
+    """Batched engine at TP=2 against the same engine at TP=1 (this process's GPU):
+    per-sequence logits slices within 1e-2, identical greedy tokens."""
+    import datetime
+    import oracle
+    from fp4x import engine, tp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    out = {}
+    try:
+        prompts = [oracle.uniform_ids(40 + i, cfg["vocab"], n) for i, n in enumerate((5, 9, 2))]
+        runs = {}
+        for mode in ("tp", "single"):
+            m = tp.create_model(cfg) if mode == "tp" else engine.Model(cfg)
+            b = tp.create_batch(m, 4) if mode == "tp" else engine.Batch(m, 4)
+            logits = []
+            for s, p in enumerate(prompts):
+                b.prefill(s, p)
+                logits.append(b.logits()[0])
+            for _ in range(5):
+                b.decode(1)
+                logits.append(b.logits()[:3])
+            toks = [b.tokens(s) for s in range(3)]
+            runs[mode] = (logits, toks, m.shard())
+            b.close()
+            m.close()
+        (lt, tt, (v0, nv)), (ls, ts, _) = runs["tp"], runs["single"]
+        worst = 0.0
+        for a, c in zip(lt, ls):
+            worst = max(worst, _rel(np.asarray(a), np.asarray(c)[..., v0:v0 + nv]))
+        out["logits_err"] = worst
+        out["tokens_equal"] = all(np.array_equal(x, y) for x, y in zip(tt, ts))
+        result[rank] = out
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_tp2_batched_engine_matches_single_gpu():
+    world = 2
+    with mp.get_context("spawn").Manager() as man:
+        result = man.dict()
+        mp.spawn(_batch_worker, args=(world, _free_port(), TINY, result), nprocs=world, join=True)
+        res = dict(result)
+    assert set(res) == {0, 1}
+    for r, out in res.items():
+        assert out["logits_err"] <= 1e-2, (r, out)
+        assert out["tokens_equal"], (r, out)
