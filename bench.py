@@ -431,6 +431,7 @@ def run_batch(args):
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     base = engine.LLAMA3_8B if args.batch_model == "llama8b" else engine.TINYLLAMA
     B, ctx = args.batch, args.batch_ctx
+    terms = 8 if os.environ.get("FP4X_BATCH_TERMS") == "8" else 4
     cfg = dict(base, max_seq=ctx + args.warmup + args.steps + 8)
     m = tp.create_model(cfg) if world > 1 else engine.Model(cfg)
     b = tp.create_batch(m, B) if world > 1 else engine.Batch(m, B)
@@ -472,7 +473,8 @@ def run_batch(args):
     line = {"metric": f"batched MXFP4 decode tok/s ({args.batch_model} shape, batch {B})", "value": B * args.steps / t,
             "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxf4 x mxf4(8-term) -> f32", "data": "synthetic (seeded N(0,0.02) weights -> MXFP4)",
+            "dtype": f"e2m1xe8m0 weights x {terms}-term e2m1xe8m0 activations on tcgen05 kind::mxf4 -> f32",
+            "data": "synthetic (seeded N(0,0.02) weights -> MXFP4)",
             "config": {"workload": "config4-batch" if args.batch_model == "llama8b" else "tinyllama-batch",
                        "batch": B, "context": ctx, "tp": world,
                        "kv": "zero-filled cache of ctx positions per sequence (prefill not timed)",
