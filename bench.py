@@ -431,7 +431,7 @@ def run_batch(args):
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     base = engine.LLAMA3_8B if args.batch_model == "llama8b" else engine.TINYLLAMA
     B, ctx = args.batch, args.batch_ctx
-    terms = 8 if os.environ.get("FP4X_BATCH_TERMS") == "8" else 4
+    terms = 4 if os.environ.get("FP4X_BATCH_TERMS") == "4" else 8
     cfg = dict(base, max_seq=ctx + args.warmup + args.steps + 8)
     m = tp.create_model(cfg) if world > 1 else engine.Model(cfg)
     b = tp.create_batch(m, B) if world > 1 else engine.Batch(m, B)

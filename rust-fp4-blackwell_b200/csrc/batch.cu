@@ -50,7 +50,7 @@ struct fp4x_llama_batch {
     float *logits = nullptr; // [rows][vocab]
     float *attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
-    uint32_t terms = 4;      // MXFP4 terms per activation row (4 or 8)
+    uint32_t terms = 8;      // MXFP4 terms per activation row (8, or 4 on request)
     uint8_t *act = nullptr, *act_s = nullptr;  // term rows [terms rows][kmax / 2], [terms rows][kmax / 32]
     float *mma_part = nullptr;  // split-K partials
     size_t mma_part_bytes = 0;
@@ -455,7 +455,7 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     fp4x_llama_batch *b = new (std::nothrow) fp4x_llama_batch();
     if (!b) return FP4X_ENOMEM;
     b->m = m, b->rows = rows, b->max_seq = c.max_seq;
-    if (const char *e = getenv("FP4X_BATCH_TERMS")) b->terms = atoi(e) == 8 ? 8 : 4;
+    if (const char *e = getenv("FP4X_BATCH_TERMS")) b->terms = atoi(e) == 4 ? 4 : 8;
     b->len.assign(rows, 0);
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     const uint32_t kmax = std::max(std::max(c.dim, c.ffn), qd);

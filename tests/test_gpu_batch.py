@@ -131,3 +131,29 @@ def test_batch_tinyllama_shape_agrees_with_batch1_engine():
             _, ref = m.forward(int(toks[pos]), pos)
             if pos >= len(prompt) - 1:
                 compare_logits(got[pos - len(prompt) + 1], ref, tol=2e-2)
+
+
+@pytest.mark.parametrize("terms,tol", [("8", 1e-2), ("4", 3e-2)])
+def test_batch_tinyllama_shape_vs_oracle(terms, tol, monkeypatch):
+    """BASELINE config-1 shape (22 layers) against the oracle: a 16-token prompt
+    prefilled in one pass, then 3 decode steps.  8-term activations (the default)
+    meet the 1e-2 logits bar (measured 2.8e-3); the opt-in 4-term mode is held to
+    its own measured bound (1.6e-2 measured, 3e-2 gate)."""
+    monkeypatch.setenv("FP4X_BATCH_TERMS", terms)
+    cfg = dict(engine.TINYLLAMA, max_seq=64)
+    prompt = oracle.uniform_ids(11, cfg["vocab"], 16)
+    ref = oracle.Model(cfg)
+    with engine.Model(cfg) as m, engine.Batch(m, 2) as b:
+        b.prefill(0, prompt)
+        got = [b.logits()[0]]
+        for _ in range(3):
+            b.decode(1)
+            got.append(b.logits()[0])
+        toks = b.tokens(0)
+    errs = []
+    for pos in range(len(prompt) + 3):
+        _, rl = ref.forward(int(toks[pos]), pos)
+        if pos >= len(prompt) - 1:
+            errs.append(compare_logits(got[pos - len(prompt) + 1], rl, tol=tol))
+    ref.close()
+    print(f"terms {terms}: max logits err {max(errs):.3e}")
