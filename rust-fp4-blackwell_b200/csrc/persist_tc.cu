@@ -385,6 +385,53 @@ __device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint3
     }
 }
 
+// The same 8-term decomposition with one value per lane (warp w: 32-blocks w,
+// w + kCW, ...; same arithmetic per value as term_words8, so the same bits), for
+// short vectors: the serial term chain per thread is 8x shorter and 8x more
+// threads share the work.  Nibbles are gathered into words by three xor-shuffles
+// within each 8-lane group.
+__device__ void decompose_lanes(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb, bool pairs) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t b = warp; b < K / 32; b += kCW) {
+        float x = v[b * 32 + lane];
+        const float a = warp_max(fabsf(x));
+        const uint32_t bits = __float_as_uint(a);
+        int e1 = (int)((bits >> 23) & 0xFFu) - 127;
+        e1 = (bits & 0x7FFFFFu) <= 0x400000u ? e1 - 2 : e1 - 1;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int e = term_exp(e1, t);
+            const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+            const float s = __uint_as_float((uint32_t)(127 + e) << 23);
+            uint32_t code;
+            asm("{\n\t.reg .b8 q0, q1;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 q1, %2, %2;\n\t"
+                "mov.b32 %0, {q0, q1, q1, q1};\n\t}"
+                : "=r"(code)
+                : "f"(x * inv), "f"(0.0f));
+            const uint32_t hv = e2m1x2_to_f16x2(code & 0xFFu);
+            const __half2 q = *reinterpret_cast<const __half2 *>(&hv);
+            x = fmaf(-__low2float(q), s, x);
+            uint32_t part = (code & 0xFu) << (4 * (lane & 7));
+            part |= __shfl_xor_sync(0xffffffffu, part, 1);
+            part |= __shfl_xor_sync(0xffffffffu, part, 2);
+            part |= __shfl_xor_sync(0xffffffffu, part, 4);
+            if ((lane & 7) == 0) *reinterpret_cast<uint32_t *>(B + b * 128 + t * 16 + (lane >> 3) * 4) = part;
+        }
+        if (lane < 8) {
+            const uint8_t sb = (uint8_t)(term_exp(e1, (int)lane) + 127);
+            if (!pairs) {
+                sfb[(b >> 2) * 128 + lane * 16 + (b & 3)] = sb;
+            } else {
+                uint8_t *q2 = sfb + (b >> 1) * 128 + lane * 16 + 2 * (b & 1);
+                q2[0] = sb;
+                q2[1] = sb;
+            }
+        }
+    }
+}
+
 // Decomposition of v[0, K) in shared memory (K % 32 == 0), one word per thread.
 __device__ void decompose8(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb, bool pairs) {
     const uint32_t nw = K / 8, lane = threadIdx.x & 31;
@@ -677,8 +724,8 @@ __device__ void fold_delta(Ctx &c, uint32_t l) {
 __device__ void o_projection(Ctx &c, uint32_t lay_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
-    decompose8(reinterpret_cast<const float *>(c.smem + c.L.xv), S.nh * p.hd, c.smem + c.L.bo, c.smem + c.L.sfbo,
-               false);
+    decompose_lanes(reinterpret_cast<const float *>(c.smem + c.L.xv), S.nh * p.hd, c.smem + c.L.bo,
+                    c.smem + c.L.sfbo, false);
     signal_operand(c, PH_O);
     CST(8);
     wait_acc(c, PH_O, lay_count & 1);
@@ -938,7 +985,7 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
         h[i] = gv / (1.0f + expf(-gv)) * uv;  // llama_run:245-253
     }
     csync();
-    decompose8(h, U, c.smem + c.L.bh, c.smem + c.L.sfbh, (U % 64) != 0);
+    decompose_lanes(h, U, c.smem + c.L.bh, c.smem + c.L.sfbh, (U % 64) != 0);
     signal_operand(c, PH_DOWN);
     CST(15);
     wait_acc(c, PH_DOWN, lay_count & 1);
