@@ -133,7 +133,7 @@ class ClockSampler:
 
 # dram__bytes_read.sum + dram__bytes_write.sum per token from one ncu capture of the
 # timed launch (profiles/decode_tc_kernel_tinyllama_bs1.md); None where not captured.
-TRAFFIC_PER_TOKEN = {"tensor": (11.331308e9 + 13.233920e6) / 20}
+TRAFFIC_PER_TOKEN = {"tensor": (11.329927e9 + 10.755072e6) / 20}
 
 DTYPES = {
     "tensor": "e2m1xe8m0 weights x 8-term e2m1xe8m0 activation on tcgen05 kind::mxf4 (exact products, "
