@@ -216,6 +216,22 @@ typedef struct fp4x_llama_model fp4x_llama_model;
  * (random weights). */
 FP4X_API int llama_model_create(const fp4x_llama_config *cfg, fp4x_llama_model **out);
 FP4X_API int llama_model_destroy(fp4x_llama_model *m);
+/* Model from a real-weight checkpoint: a safetensors file with Hugging Face Llama
+ * tensor names (model.embed_tokens.weight, model.layers.N.self_attn.{q,k,v,o}_proj
+ * .weight, model.layers.N.mlp.{gate,up,down}_proj.weight, model.layers.N.
+ * {input,post_attention}_layernorm.weight, model.norm.weight, lm_head.weight or tied
+ * embeddings), dtypes F32 / BF16 / F16, shapes matching cfg.  Every linear is
+ * quantised to MXFP4 on the GPU (the fp4_quantize_mxfp4 rule), embeddings kept as
+ * bf16, norm weights f32; under tensor parallelism each rank reads its shard.
+ * Replaces the reference's loading and host quantisation, llama_run/src/main.rs:
+ * 413-460 (f16/bf16 widening :425-427, :591-614; quant_fp4 :334-376). */
+FP4X_API int llama_model_create_from_safetensors(const fp4x_llama_config *cfg, const char *path,
+                                                 fp4x_llama_model **out);
+/* Host-only: dtype (0 F32, 1 BF16, 2 F16, -1 other), rank and shape (up to 8 dims)
+ * of tensor `name` in a safetensors file; FP4X_EINVAL if the file is malformed or
+ * the tensor is absent. */
+FP4X_API int fp4x_safetensors_info(const char *path, const char *name, uint32_t *dtype_out, uint64_t *shape_out,
+                                   uint32_t *ndim_out);
 /* Zero the KV cache. */
 FP4X_API int llama_model_reset(fp4x_llama_model *m, fp4x_stream_t stream);
 /* forward(tok, pos) -> next token, llama_run/src/main.rs:492-536: one token at

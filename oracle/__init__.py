@@ -99,6 +99,9 @@ def _declare(L):
         "orc_model_packed": (_u8p, [C.c_void_p, C.c_uint32]),
         "orc_model_scales": (_u8p, [C.c_void_p, C.c_uint32]),
         "orc_model_embed": (_u16p, [C.c_void_p]),
+        "orc_model_set_tensor": (None, [C.c_void_p, C.c_uint32, _u8p, _u8p]),
+        "orc_model_set_embed": (None, [C.c_void_p, _u16p]),
+        "orc_model_set_norm": (None, [C.c_void_p, C.c_uint32, _f32p]),
         "orc_forward": (C.c_uint32, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
         "orc_generate": (None, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p]),
         "orc_max_threads": (C.c_int, []),
@@ -326,6 +329,18 @@ class Model:
         packed = np.ctypeslib.as_array(p, shape=(n * k // 2,)).reshape(n, k // 2).copy()
         scales = np.ctypeslib.as_array(s, shape=(n * k // 32,)).reshape(n, k // 32).copy()
         return packed, scales
+
+    def set_tensor(self, tensor_id: int, packed, scales):
+        """Replace a linear (canonical MXFP4 layout) -- checkpoint-loader tests."""
+        lib().orc_model_set_tensor(self._h, tensor_id, _p(np.ascontiguousarray(packed, np.uint8), C.c_uint8),
+                                   _p(np.ascontiguousarray(scales, np.uint8), C.c_uint8))
+
+    def set_embed(self, embed_bf16):
+        lib().orc_model_set_embed(self._h, _p(np.ascontiguousarray(embed_bf16, np.uint16), C.c_uint16))
+
+    def set_norm(self, which: int, w):
+        """which: 0..L-1 attention norm, L..2L-1 FFN norm, 2L final norm."""
+        lib().orc_model_set_norm(self._h, which, _p(np.ascontiguousarray(w, np.float32), C.c_float))
 
     def embed(self):
         p = lib().orc_model_embed(self._h)

@@ -446,6 +446,7 @@ struct orc_model {
     qmat *lin; /* [n_layers * 7] */
     qmat lm_head;
     uint16_t *embed;
+    float *norms;      /* [2 n_layers + 1][dim]: attention norms, FFN norms, final norm (ones) */
     uint16_t *kc, *vc; /* [n_layers][max_seq][n_kv][hd] bf16 */
     float *cos_t, *sin_t;
     float *x, *h, *q, *k, *v, *a, *ao, *g, *u, *s, *d, *logits;
@@ -499,6 +500,8 @@ orc_model *orc_model_create(const orc_config *cfg, int threads) {
     size_t ne = (size_t)c->vocab * c->dim;
     m->embed = (uint16_t *)malloc(ne * 2);
     orc_fill_normal_bf16(orc_hash64(c->seed, T_EMBED), 0, 0.02f, m->embed, ne);
+    m->norms = (float *)malloc(sizeof(float) * (2 * (size_t)c->n_layers + 1) * c->dim);
+    for (size_t i = 0; i < (2 * (size_t)c->n_layers + 1) * c->dim; ++i) m->norms[i] = 1.0f;
     size_t kvn = (size_t)c->n_layers * c->max_seq * c->n_kv_heads * c->head_dim;
     m->kc = (uint16_t *)calloc(kvn, 2);
     m->vc = (uint16_t *)calloc(kvn, 2);
@@ -523,6 +526,7 @@ orc_model *orc_model_create(const orc_config *cfg, int threads) {
 
 void orc_model_destroy(orc_model *m) {
     if (!m) return;
+    free(m->norms);
     for (uint32_t i = 0; i < m->c.n_layers * M_COUNT; ++i) {
         free(m->lin[i].packed);
         free(m->lin[i].scales);
@@ -558,6 +562,22 @@ const uint8_t *orc_model_scales(const orc_model *m, uint32_t id) {
 
 const uint16_t *orc_model_embed(const orc_model *m) { return m->embed; }
 
+/* Replace model weights (tests of the checkpoint loader): tensor_id as in
+ * orc_model_packed, canonical [n][k/2] nibbles + [n][k/32] E8M0 scales. */
+void orc_model_set_tensor(orc_model *m, uint32_t tensor_id, const uint8_t *packed, const uint8_t *scales) {
+    qmat *q = tensor_id == 1 ? &m->lm_head : &m->lin[((tensor_id - 16) / 8) * M_COUNT + (tensor_id - 16) % 8];
+    memcpy(q->packed, packed, (size_t)q->n * q->k / 2);
+    memcpy(q->scales, scales, (size_t)q->n * q->k / 32);
+}
+void orc_model_set_embed(orc_model *m, const uint16_t *embed) {
+    memcpy(m->embed, embed, (size_t)m->c.vocab * m->c.dim * 2);
+}
+/* which: 0..L-1 attention norm of layer which, L..2L-1 FFN norm of layer which-L,
+ * 2L the final norm (llama_run/src/main.rs:79-116 weight vector). */
+void orc_model_set_norm(orc_model *m, uint32_t which, const float *w) {
+    memcpy(m->norms + (size_t)which * m->c.dim, w, sizeof(float) * m->c.dim);
+}
+
 static void lin(orc_model *m, const qmat *w, const float *x, float *y) {
     orc_gemv_mxfp4(w->n, w->k, w->packed, w->scales, x, y, m->threads);
 }
@@ -573,12 +593,10 @@ uint32_t orc_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits) 
     for (uint32_t i = 0; i < c->dim; ++i) m->x[i] = orc_bf16_to_f32(er[i]);
     float *kf = (float *)malloc(sizeof(float) * (size_t)seq * kvd);
     float *vf = (float *)malloc(sizeof(float) * (size_t)seq * kvd);
-    float *ones = (float *)malloc(sizeof(float) * c->dim);
-    for (uint32_t i = 0; i < c->dim; ++i) ones[i] = 1.0f;
     uint32_t cos_base = pos * half;
     for (uint32_t l = 0; l < c->n_layers; ++l) {
         qmat *L = &m->lin[l * M_COUNT];
-        orc_rmsnorm(c->dim, c->eps, m->x, ones, m->h);
+        orc_rmsnorm(c->dim, c->eps, m->x, m->norms + (size_t)l * c->dim, m->h);
         lin(m, &L[M_Q], m->h, m->q);
         lin(m, &L[M_K], m->h, m->k);
         lin(m, &L[M_V], m->h, m->v);
@@ -597,18 +615,17 @@ uint32_t orc_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits) 
         orc_attn_decode(nh, nkv, hd, seq, m->q, kf, vf, m->a, m->threads);
         lin(m, &L[M_O], m->a, m->ao);
         orc_residual(c->dim, m->ao, m->x);
-        orc_rmsnorm(c->dim, c->eps, m->x, ones, m->h);
+        orc_rmsnorm(c->dim, c->eps, m->x, m->norms + (size_t)(c->n_layers + l) * c->dim, m->h);
         lin(m, &L[M_GATE], m->h, m->g);
         lin(m, &L[M_UP], m->h, m->u);
         orc_swiglu(c->ffn, m->g, m->u, m->s);
         lin(m, &L[M_DOWN], m->s, m->d);
         orc_residual(c->dim, m->d, m->x);
     }
-    orc_rmsnorm(c->dim, c->eps, m->x, ones, m->h);
+    orc_rmsnorm(c->dim, c->eps, m->x, m->norms + (size_t)2 * c->n_layers * c->dim, m->h);
     lin(m, &m->lm_head, m->h, m->logits);
     free(kf);
     free(vf);
-    free(ones);
     if (logits) memcpy(logits, m->logits, sizeof(float) * c->vocab);
     return orc_argmax(c->vocab, m->logits);
 }

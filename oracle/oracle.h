@@ -130,6 +130,12 @@ void orc_model_destroy(orc_model *m);
 const uint8_t *orc_model_packed(const orc_model *m, uint32_t tensor_id);
 const uint8_t *orc_model_scales(const orc_model *m, uint32_t tensor_id);
 const uint16_t *orc_model_embed(const orc_model *m);
+/* Replace weights (checkpoint-loader tests): a linear (tensor_id as above, canonical
+ * layout), the bf16 embeddings, or a norm weight vector (which: 0..L-1 attention,
+ * L..2L-1 FFN, 2L final; ones after orc_model_create). */
+void orc_model_set_tensor(orc_model *m, uint32_t tensor_id, const uint8_t *packed, const uint8_t *scales);
+void orc_model_set_embed(orc_model *m, const uint16_t *embed);
+void orc_model_set_norm(orc_model *m, uint32_t which, const float *w);
 /* One token through the model at `pos` (llama_run/src/main.rs:509-535); writes
  * logits[vocab] and returns the argmax (UINT32_MAX, nothing written, if pos >=
  * max_seq or token >= vocab). */

@@ -371,7 +371,10 @@ int build_persistent(fp4x_llama_model *m, const ptc::TpIn *tpin) {
     return rc;
 }
 
-int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
+int load_safetensors(fp4x_llama_model *m, cudaStream_t st, const char *path);  // loader.cu
+
+// weights_path: a safetensors checkpoint to load instead of the seeded init.
+int create(const fp4x_llama_config *cfg, fp4x_llama_model **out, const char *weights_path = nullptr) {
     FP4X_REQUIRE(cfg && out, "llama_model_create: null pointer");
     FP4X_TRY(validate_config(*cfg));
     fp4x_llama_model *m = new (std::nothrow) fp4x_llama_model();
@@ -427,7 +430,7 @@ int create(const fp4x_llama_config *cfg, fp4x_llama_model **out) {
     if (rc) return fail(rc);
     if (cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking) != cudaSuccess)
         return fail(cuda_fail("cudaStreamCreate", cudaGetLastError()));
-    rc = init_weights(m, m->cap_stream);
+    rc = weights_path ? load_safetensors(m, m->cap_stream, weights_path) : init_weights(m, m->cap_stream);
     if (!rc) {
         const uint32_t st[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (cudaMemcpyAsync(m->state, st, sizeof(st), cudaMemcpyHostToDevice, m->cap_stream) != cudaSuccess ||

@@ -10,4 +10,5 @@
 #include "persist_tc.cu"
 #include "tp.cu"
 #include "engine.cu"
+#include "loader.cu"
 #include "batch.cu"

@@ -47,6 +47,8 @@ SIGNATURES = {
     "llama_model_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "llama_model_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "llama_model_shard": (C.c_int, [C.c_void_p, _u32p, _u32p]),
+    "llama_model_create_from_safetensors": (C.c_int, [C.POINTER(Config), C.c_char_p, C.POINTER(C.c_void_p)]),
+    "fp4x_safetensors_info": (C.c_int, [C.c_char_p, C.c_char_p, _u32p, C.POINTER(C.c_uint64), _u32p]),
     "llama_batch_create": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
     "llama_batch_destroy": (C.c_int, [C.c_void_p]),
     "llama_batch_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, _u32p, C.c_uint32]),
@@ -76,7 +78,9 @@ def _p(a, ct):
 class Model:
     """A random-init Llama-shape MXFP4 model on the current CUDA device."""
 
-    def __init__(self, cfg: dict, stream: int | None = None):
+    def __init__(self, cfg: dict, stream: int | None = None, safetensors: str | None = None):
+        """Random-init weights from cfg["seed"], or the checkpoint at `safetensors`
+        (llama_model_create_from_safetensors; Hugging Face Llama tensor names)."""
         self.L = _declare()
         self.cfg = dict(cfg)
         c = Config(**{k: self.cfg.get(k, 0) for k, _ in Config._fields_})
@@ -84,7 +88,10 @@ class Model:
             c.tp_size = 1
         self._c = c
         h = C.c_void_p()
-        check(self.L.llama_model_create(C.byref(c), C.byref(h)))
+        if safetensors is None:
+            check(self.L.llama_model_create(C.byref(c), C.byref(h)))
+        else:
+            check(self.L.llama_model_create_from_safetensors(C.byref(c), str(safetensors).encode(), C.byref(h)))
         self._h = h
         self.stream = stream
 
@@ -248,3 +255,13 @@ class Batch:
         """Map every rank's batch exchange area (handles in rank order)."""
         blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
         check(self.L.llama_batch_tp_connect(self._h, blob))
+
+
+def safetensors_info(path: str, name: str):
+    """(dtype tag, shape) of one tensor of a safetensors file (host only)."""
+    L = _declare()
+    dt, nd = C.c_uint32(0), C.c_uint32(0)
+    shape = (C.c_uint64 * 8)()
+    check(L.fp4x_safetensors_info(str(path).encode(), name.encode(), C.byref(dt), shape, C.byref(nd)))
+    tag = {0: "F32", 1: "BF16", 2: "F16"}.get(C.c_int32(dt.value).value, "other")
+    return tag, tuple(int(shape[i]) for i in range(nd.value))

@@ -31,12 +31,13 @@ def exchange_handles(handle: bytes, group=None) -> list[bytes]:
     return out
 
 
-def create_model(cfg: dict, group=None):
-    """Create this rank's shard of `cfg` and connect it to the other ranks."""
+def create_model(cfg: dict, group=None, safetensors: str | None = None):
+    """Create this rank's shard of `cfg` (random init, or read from a safetensors
+    checkpoint) and connect it to the other ranks."""
     import torch.distributed as dist
     from .engine import Model
     rank, world = dist.get_rank(group), dist.get_world_size(group)
-    m = Model(dict(cfg, tp_rank=rank, tp_size=world))
+    m = Model(dict(cfg, tp_rank=rank, tp_size=world), safetensors=safetensors)
     if world > 1:
         m.tp_connect(exchange_handles(m.tp_handle(), group))
     return m
