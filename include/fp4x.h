@@ -118,6 +118,23 @@ FP4X_API int fp4_mma(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, c
  * K split: one CTA per output tile). */
 FP4X_API int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
                          const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float *d);
+/* NVFP4 form of the same GEMM (the reference's kind::mxf4nvf4 / scale_vec::4X /
+ * .ue4m3 variant, trackb/FP4_M16N8K64_LAYOUT.md:7): E2M1 operands with one unsigned
+ * E4M3 scale per 16 values ([rows][k/16] bytes), d = alpha * A W^T (alpha carries
+ * the operands' per-tensor scales).  Runs tcgen05.mma.kind::mxf4nvf4.block16. */
+FP4X_API size_t fp4_mma_nvf4_workspace_size(uint32_t m, uint32_t n, uint32_t k);
+FP4X_API int fp4_mma_nvf4(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                          const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float alpha,
+                          uint16_t *d_bf16, void *workspace, size_t workspace_bytes);
+FP4X_API int fp4_mma_nvf4_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                              const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float alpha,
+                              float *d);
+/* NVFP4 quantiser: per 16-block s = amax / 6 / global_scale rounded to the nearest
+ * UE4M3 (ties to even, saturating at 448), values / (UE4M3(s) * global_scale)
+ * rounded to E2M1 with the reference's tie rule (llama_run/src/main.rs:350-362).
+ * k % 16 == 0; packed [n][k/2], scales [n][k/16]. */
+FP4X_API int fp4_quantize_nvfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w, uint8_t *packed,
+                                uint8_t *scales, float global_scale);
 /* The reference's known-answer test on the tcgen05 path: A = B = all 1.0
  * (bytes 0x22), every scale 2^0 (0x7F), K = 64; out[16*8] = D, every value 64.0.
  * Replaces fp4_mma_allones, examples/fp4_mma/src/main.rs:18-54 (check :75-85). */

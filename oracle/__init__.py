@@ -100,6 +100,11 @@ def _declare(L):
         "orc_model_scales": (_u8p, [C.c_void_p, C.c_uint32]),
         "orc_model_embed": (_u16p, [C.c_void_p]),
         "orc_model_set_tensor": (None, [C.c_void_p, C.c_uint32, _u8p, _u8p]),
+        "orc_ue4m3_to_f32": (C.c_float, [C.c_uint8]),
+        "orc_f32_to_ue4m3": (C.c_uint8, [C.c_float]),
+        "orc_quant_nvfp4": (None, [_f32p, C.c_size_t, C.c_size_t, _u8p, _u8p, C.c_float]),
+        "orc_mma_nvf4": (None, [C.c_uint32, C.c_uint32, C.c_uint32, _u8p, _u8p, _u8p, _u8p, C.c_float, _f32p,
+                                C.c_int]),
         "orc_model_set_embed": (None, [C.c_void_p, _u16p]),
         "orc_model_set_norm": (None, [C.c_void_p, C.c_uint32, _f32p]),
         "orc_forward": (C.c_uint32, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
@@ -286,6 +291,35 @@ def mma_mxf4(a, sa, w, sw, threads=0):
                        _p(np.ascontiguousarray(sa, np.uint8), C.c_uint8),
                        _p(np.ascontiguousarray(w, np.uint8), C.c_uint8),
                        _p(np.ascontiguousarray(sw, np.uint8), C.c_uint8), _p(d, C.c_float), threads)
+    return d
+
+
+# ---------------------------------------------------------------- NVFP4
+
+def ue4m3_to_f32(b: int) -> float:
+    return float(lib().orc_ue4m3_to_f32(int(b)))
+
+
+def f32_to_ue4m3(s: float) -> int:
+    return int(lib().orc_f32_to_ue4m3(float(s)))
+
+
+def quant_nvfp4(w: np.ndarray, g: float = 1.0):
+    """f32 [n][k] -> (packed [n][k/2], UE4M3 scales [n][k/16]) with per-tensor scale g."""
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    packed = np.empty((n, k // 2), np.uint8)
+    scales = np.empty((n, k // 16), np.uint8)
+    lib().orc_quant_nvfp4(_p(w, C.c_float), n, k, _p(packed, C.c_uint8), _p(scales, C.c_uint8), g)
+    return packed, scales
+
+
+def mma_nvf4(a, sa, w, sw, alpha: float = 1.0, threads: int = 0):
+    m, n, k = a.shape[0], w.shape[0], a.shape[1] * 2
+    d = np.empty((m, n), np.float32)
+    lib().orc_mma_nvf4(m, n, k, _p(np.ascontiguousarray(a, np.uint8), C.c_uint8),
+                       _p(np.ascontiguousarray(sa, np.uint8), C.c_uint8), _p(np.ascontiguousarray(w, np.uint8), C.c_uint8),
+                       _p(np.ascontiguousarray(sw, np.uint8), C.c_uint8), alpha, _p(d, C.c_float), threads)
     return d
 
 

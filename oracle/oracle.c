@@ -429,6 +429,75 @@ void orc_mma_mxf4(uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const ui
         }
 }
 
+/* ------------------------------------------------------------- NVFP4 */
+/* NVFP4 (the reference's kind::mxf4nvf4 / scale_vec::4X / .ue4m3 variant,
+ * trackb/FP4_M16N8K64_LAYOUT.md:7, trackb/nvf4_m16n8k64_template.ptx): E2M1 codes
+ * with one unsigned E4M3 scale per 16 values and a per-tensor f32 scale g.  The
+ * reference ships no quantiser for it; this library's rule, shared bit for bit
+ * with the device: per 16-block s = amax / 6 / g rounded to the nearest UE4M3
+ * (ties to even, saturating at 448, zero for s <= 0), then each value divided by
+ * UE4M3(s) * g and rounded to E2M1 with the reference's tie rule (quant_fp4,
+ * llama_run/src/main.rs:350-362). */
+float orc_ue4m3_to_f32(uint8_t b) {
+    uint32_t e = (b >> 3) & 15u, m = b & 7u;
+    return e == 0 ? ldexpf((float)m, -9) : ldexpf((float)(8u + m), (int)e - 10);
+}
+
+uint8_t orc_f32_to_ue4m3(float s) {
+    if (!(s > 0.0f)) return 0;
+    if (s >= 448.0f) return 0x7E;
+    if (s < 0.015625f) { /* below 2^-6: subnormal step 2^-9 */
+        float m = rintf(s * 512.0f);
+        return (uint8_t)m; /* m == 8 is the smallest normal, 0x08 */
+    }
+    uint32_t bits;
+    memcpy(&bits, &s, 4);
+    int e = (int)((bits >> 23) & 0xFFu) - 127;
+    float mant = ldexpf(s, -e) - 1.0f; /* exact */
+    int E = e + 7, m = (int)rintf(mant * 8.0f);
+    if (m == 8) E += 1, m = 0;
+    if (E > 15 || (E == 15 && m == 7)) return 0x7E;
+    return (uint8_t)((E << 3) | m);
+}
+
+void orc_quant_nvfp4(const float *w, size_t n, size_t k, uint8_t *packed, uint8_t *scales, float g) {
+    size_t nb = k / 16;
+    for (size_t r = 0; r < n; ++r)
+        for (size_t b = 0; b < nb; ++b) {
+            size_t base = r * k + b * 16;
+            float amax = 0.0f;
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(w[base + i]));
+            uint8_t S = orc_f32_to_ue4m3(amax / 6.0f / g);
+            float eff = orc_ue4m3_to_f32(S) * g;
+            scales[r * nb + b] = S;
+            for (int i = 0; i < 16; i += 2) {
+                uint32_t lo = eff > 0.0f ? orc_e2m1_nearest(w[base + i] / eff) : 0u;
+                uint32_t hi = eff > 0.0f ? orc_e2m1_nearest(w[base + i + 1] / eff) : 0u;
+                packed[base / 2 + i / 2] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+}
+
+/* d[t][r] = alpha * sum_k e2m1(A[t][k]) UE4M3(SA[t][k/16]) e2m1(W[r][k]) UE4M3(SW[r][k/16]). */
+void orc_mma_nvf4(uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa, const uint8_t *w,
+                  const uint8_t *sw, float alpha, float *d, int threads) {
+    ensure_lut();
+    uint32_t kb = k / 16;
+#pragma omp parallel for schedule(static) num_threads(nthreads(threads))
+    for (uint32_t i = 0; i < m; ++i)
+        for (uint32_t j = 0; j < n; ++j) {
+            float s = 0.0f;
+            for (uint32_t kk = 0; kk < k; ++kk) {
+                uint8_t ab = a[((size_t)i * k + kk) / 2], wb = w[((size_t)j * k + kk) / 2];
+                float av = decode_lut[(kk & 1) ? (ab >> 4) : (ab & 0xF)];
+                float wv = decode_lut[(kk & 1) ? (wb >> 4) : (wb & 0xF)];
+                s += av * orc_ue4m3_to_f32(sa[(size_t)i * kb + kk / 16]) * wv *
+                     orc_ue4m3_to_f32(sw[(size_t)j * kb + kk / 16]);
+            }
+            d[(size_t)i * n + j] = alpha * s;
+        }
+}
+
 /* --------------------------------------------------------------- model */
 
 enum { T_EMBED = 0, T_LMHEAD = 1, T_LAYER0 = 16 };

@@ -118,6 +118,13 @@ typedef struct {
     uint64_t seed;
 } orc_config;
 
+/* NVFP4: E2M1 with an unsigned-E4M3 scale per 16 values and a per-tensor f32 g. */
+float orc_ue4m3_to_f32(uint8_t b);
+uint8_t orc_f32_to_ue4m3(float s);
+void orc_quant_nvfp4(const float *w, size_t n, size_t k, uint8_t *packed, uint8_t *scales, float g);
+void orc_mma_nvf4(uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa, const uint8_t *w,
+                  const uint8_t *sw, float alpha, float *d, int threads);
+
 typedef struct orc_model orc_model;
 
 /* Random-init model, generated with the same tensor seeds as the device initialiser:

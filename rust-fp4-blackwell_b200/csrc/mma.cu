@@ -63,23 +63,26 @@ constexpr uint32_t kBarBytes = 256;
 // destination (a residual; one writer per element, so a plain load + store).
 enum Mode : uint32_t { OUT_BF16 = 0, OUT_F32 = 1, OUT_ADD_F32 = 2 };
 
+// ak = scale atoms per 256-k stage per 128 rows: 2 for MXFP4 (E8M0 per 32, an atom
+// row holds 4 blocks = 128 k), 4 for NVFP4 (UE4M3 per 16, an atom row = 64 k).
 struct Geo {
-    uint32_t nt, stages, sfb_atoms, stage_bytes, b_off, sfa_off, sfb_off, tmem_cols, sfa_col0, sfb_col0, smem;
+    uint32_t nt, ak, stages, sfb_atoms, stage_bytes, b_off, sfa_off, sfb_off, tmem_cols, sfa_col0, sfb_col0, smem;
 };
 
-__host__ __device__ inline Geo geometry(uint32_t nt) {
+__host__ __device__ inline Geo geometry(uint32_t nt, bool nv = false) {
     Geo g;
     g.nt = nt;
+    g.ak = nv ? 4 : 2;
     g.sfb_atoms = nt > 128 ? 2 : 1;
     g.b_off = kTileA;
     g.sfa_off = g.b_off + nt * 128;
-    g.sfb_off = g.sfa_off + 2 * 512;
-    g.stage_bytes = (g.sfb_off + g.sfb_atoms * 2 * 512 + 1023) / 1024 * 1024;
+    g.sfb_off = g.sfa_off + g.ak * 512;
+    g.stage_bytes = (g.sfb_off + g.sfb_atoms * g.ak * 512 + 1023) / 1024 * 1024;
     uint32_t s = (kSmemLimit - 1024 - kBarBytes) / g.stage_bytes;
     g.stages = s > kMaxStages ? kMaxStages : s;
     g.sfa_col0 = nt;
-    g.sfb_col0 = nt + g.stages * 8;
-    const uint32_t cols = g.sfb_col0 + g.stages * 8 * g.sfb_atoms;
+    g.sfb_col0 = nt + g.stages * 4 * g.ak;
+    const uint32_t cols = g.sfb_col0 + g.stages * 4 * g.ak * g.sfb_atoms;
     uint32_t c = 32;
     while (c < cols) c *= 2;
     g.tmem_cols = c;
@@ -95,6 +98,7 @@ struct Args {
     uint32_t terms;             // 1, 4 or 8: A rows T t .. T t + T - 1 are the MXFP4 terms of token t (summed)
     uint32_t splits;            // K splits (blockIdx.z); > 1: partial sums to ws, added by splitk_reduce_kernel
     float *ws;                  // [splits][m / terms][n] partial sums
+    float alpha;                // output multiplier (NVFP4 per-tensor scales; 1 for MXFP4)
 };
 
 __device__ __forceinline__ void emit(const Args &a, uint32_t tok, uint32_t row, float v) {
@@ -155,6 +159,7 @@ __device__ void epilogue_sums(const Args &a, uint32_t tbase, uint32_t q, uint32_
                 float sum = v[u][j];
 #pragma unroll
                 for (uint32_t e = 1; e < T; ++e) sum += v[u][j + e];
+                sum *= a.alpha;
                 const uint32_t tk = (tok0 + c0 + 8 * u + j) / T;
                 if (!row_ok || tk >= tokens) continue;
                 if (a.splits > 1)
@@ -190,11 +195,26 @@ __device__ __forceinline__ uint2 load_scales8(const uint8_t *s, uint32_t row, ui
     return make_uint2(w[0], w[1]);
 }
 
+// 16 scale bytes [kb0, kb0 + 16) of one row (0 outside the matrix).
+__device__ __forceinline__ uint4 load_scales16(const uint8_t *s, uint32_t row, uint32_t rows, uint32_t kb0,
+                                               uint32_t kbt) {
+    if (row >= rows) return make_uint4(0, 0, 0, 0);
+    const uint8_t *p = s + (size_t)row * kbt + kb0;
+    if ((kbt & 15u) == 0 && kb0 + 16 <= kbt) return __ldg(reinterpret_cast<const uint4 *>(p));
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (uint32_t j = 0; j < 16; ++j)
+        if (kb0 + j < kbt) w[j >> 2] |= (uint32_t)__ldg(p + j) << (8 * (j & 3));
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// NV: NVFP4 operands (UE4M3 scales per 16, kind::mxf4nvf4); otherwise MXFP4.
+template <bool NV>
 __global__ void __launch_bounds__(kThreads, 1)
     mxf4_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a, Args a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const Geo G = geometry(a.nt);
+    const Geo G = geometry(a.nt, NV);
     const uint32_t S = G.stages;
     uint64_t *full_t = reinterpret_cast<uint64_t *>(smem + S * G.stage_bytes);  // TMA bytes landed
     uint64_t *full_s = full_t + kMaxStages;                                     // scale atoms written
@@ -205,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t tok0 = blockIdx.x * a.nt, row0 = blockIdx.y * 128;
-    const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / 32;
+    const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / (NV ? 16 : 32);
     const uint32_t s0 = blockIdx.z * a.kps, s1 = min(kst, s0 + a.kps);
     const uint32_t nst = s1 > s0 ? s1 - s0 : 0;
     // CTAs walk their K stages in rotated order (start = weight tile index mod
@@ -255,28 +275,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = tc::idesc_mxf4(a.nt);
+            const uint32_t idesc = NV ? tc::idesc_nvf4(a.nt) : tc::idesc_mxf4(a.nt);
             for (uint32_t i = 0; i < nst; ++i) {
                 const uint32_t slot = i % S, par = (i / S) & 1;
                 if (!wait_or_abort(&full_t[slot], par, abort) || !wait_or_abort(&full_s[slot], par, abort)) break;
                 tc::fence_after_sync();
                 const uint8_t *st = smem + slot * G.stage_bytes;
-                const uint32_t sa_col = tbase + G.sfa_col0 + slot * 8;
-                const uint32_t sb_col = tbase + G.sfb_col0 + slot * 8 * G.sfb_atoms;
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {  // K = 128 halves of the stage
-                    tc::utccp_scale_atom(sa_col + 4 * h, tc::desc_scale_atom(smem_u32(st + G.sfa_off + h * 512)));
+                const uint32_t sa_col = tbase + G.sfa_col0 + slot * 4 * G.ak;
+                const uint32_t sb_col = tbase + G.sfb_col0 + slot * 4 * G.ak * G.sfb_atoms;
+                for (uint32_t at = 0; at < G.ak; ++at) {  // atom at covers k [at, at + 1) x 256 / ak of the stage
+                    tc::utccp_scale_atom(sa_col + 4 * at, tc::desc_scale_atom(smem_u32(st + G.sfa_off + at * 512)));
                     for (uint32_t q = 0; q < G.sfb_atoms; ++q)
-                        tc::utccp_scale_atom(sb_col + h * 4 * G.sfb_atoms + 4 * q,
-                                             tc::desc_scale_atom(smem_u32(st + G.sfb_off + (q * 2 + h) * 512)));
+                        tc::utccp_scale_atom(sb_col + at * 4 * G.sfb_atoms + 4 * q,
+                                             tc::desc_scale_atom(smem_u32(st + G.sfb_off + (q * G.ak + at) * 512)));
                 }
                 const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + G.b_off);
 #pragma unroll
                 for (uint32_t kk = 0; kk < 4; ++kk) {
-                    const uint32_t h = kk >> 1, sid = (kk & 1) * 2;
-                    tc::mma_mxf4(tbase, tc::desc_sw128(a_addr + 32 * kk), tc::desc_sw128(b_addr + 32 * kk), idesc,
-                                 (sa_col + 4 * h) | (sid << 30), (sb_col + h * 4 * G.sfb_atoms) | (sid << 30),
-                                 (i | kk) != 0);
+                    const uint64_t ad = tc::desc_sw128(a_addr + 32 * kk), bd = tc::desc_sw128(b_addr + 32 * kk);
+                    if constexpr (NV) {  // one atom (4 UE4M3 bytes per row) per K=64
+                        tc::mma_nvf4(tbase, ad, bd, idesc, sa_col + 4 * kk, sb_col + kk * 4 * G.sfb_atoms, (i | kk) != 0);
+                    } else {  // one atom per K=128, scale ids 0/2 pick its byte pair
+                        const uint32_t h = kk >> 1, sid = (kk & 1) * 2;
+                        tc::mma_mxf4(tbase, ad, bd, idesc, (sa_col + 4 * h) | (sid << 30),
+                                     (sb_col + h * 4 * G.sfb_atoms) | (sid << 30), (i | kk) != 0);
+                    }
                 }
                 tc::commit(&empty[slot]);
             }
@@ -288,14 +311,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ring shifted every stage), so the global-load latency overlaps the MMAs
         // of the stages in between instead of adding to every stage.
         constexpr uint32_t kScaleAhead = 4;
-        uint2 rw[kScaleAhead], rb0[kScaleAhead], rb1[kScaleAhead];
-        auto fetch = [&](uint32_t i, uint2 &w, uint2 &b0, uint2 &b1) {
-            w = b0 = b1 = make_uint2(0, 0);
+        uint4 rw[kScaleAhead], rb0[kScaleAhead], rb1[kScaleAhead];
+        auto load = [&](const uint8_t *sc, uint32_t row, uint32_t rows, uint32_t kb0) {
+            if constexpr (NV) return load_scales16(sc, row, rows, kb0, kbt);
+            const uint2 v = load_scales8(sc, row, rows, kb0, kbt);
+            return make_uint4(v.x, v.y, 0u, 0u);
+        };
+        auto fetch = [&](uint32_t i, uint4 &w, uint4 &b0, uint4 &b1) {
+            w = b0 = b1 = make_uint4(0, 0, 0, 0);
             if (i >= nst) return;
-            const uint32_t kb0 = stage_of(i) * 8;
-            w = load_scales8(a.sw, row0 + t, a.n, kb0, kbt);
-            if (t < a.nt) b0 = load_scales8(a.sa, tok0 + t, a.m, kb0, kbt);
-            if (G.sfb_atoms > 1 && t + 128 < a.nt) b1 = load_scales8(a.sa, tok0 + t + 128, a.m, kb0, kbt);
+            const uint32_t kb0 = stage_of(i) * (NV ? 16 : 8);
+            w = load(a.sw, row0 + t, a.n, kb0);
+            if (t < a.nt) b0 = load(a.sa, tok0 + t, a.m, kb0);
+            if (G.sfb_atoms > 1 && t + 128 < a.nt) b1 = load(a.sa, tok0 + t + 128, a.m, kb0);
         };
 #pragma unroll
         for (uint32_t j = 0; j < kScaleAhead; ++j) fetch(j, rw[j], rb0[j], rb1[j]);
@@ -304,13 +332,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
             uint8_t *st = smem + slot * G.stage_bytes;
             const uint32_t off = tc::scale_atom_off(t, 0);
-            *reinterpret_cast<uint32_t *>(st + G.sfa_off + off) = rw[0].x;
-            *reinterpret_cast<uint32_t *>(st + G.sfa_off + 512 + off) = rw[0].y;
-            *reinterpret_cast<uint32_t *>(st + G.sfb_off + off) = rb0[0].x;
-            *reinterpret_cast<uint32_t *>(st + G.sfb_off + 512 + off) = rb0[0].y;
-            if (G.sfb_atoms > 1) {
-                *reinterpret_cast<uint32_t *>(st + G.sfb_off + 1024 + off) = rb1[0].x;
-                *reinterpret_cast<uint32_t *>(st + G.sfb_off + 1536 + off) = rb1[0].y;
+            const uint32_t wa[4] = {rw[0].x, rw[0].y, rw[0].z, rw[0].w};
+            const uint32_t wb0[4] = {rb0[0].x, rb0[0].y, rb0[0].z, rb0[0].w};
+            const uint32_t wb1[4] = {rb1[0].x, rb1[0].y, rb1[0].z, rb1[0].w};
+#pragma unroll
+            for (uint32_t at = 0; at < (NV ? 4u : 2u); ++at) {
+                *reinterpret_cast<uint32_t *>(st + G.sfa_off + at * 512 + off) = wa[at];
+                *reinterpret_cast<uint32_t *>(st + G.sfb_off + at * 512 + off) = wb0[at];
+                if (G.sfb_atoms > 1) *reinterpret_cast<uint32_t *>(st + G.sfb_off + (G.ak + at) * 512 + off) = wb1[at];
             }
             fence_proxy_async_smem();
             mbar_arrive(&full_s[slot]);
@@ -404,7 +433,7 @@ struct Plan {
     Geo g;
 };
 
-inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true) {
+inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true, bool nv = false) {
     Plan p;
     p.nt = m >= 256 ? 256 : (m + 7) / 8 * 8;
     p.m_tiles = (m + p.nt - 1) / p.nt;
@@ -422,7 +451,7 @@ inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true) {
     }
     p.kps = (p.kst + splits - 1) / splits;
     p.splits = (p.kst + p.kps - 1) / p.kps;
-    p.g = geometry(p.nt);
+    p.g = geometry(p.nt, nv);
     return p;
 }
 
@@ -443,7 +472,8 @@ inline size_t partials_bytes(const Plan &p, uint32_t m, uint32_t n, uint32_t ter
 
 // partials: split-K scratch of partials_bytes() (unused when p.splits == 1).
 int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa,
-           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms, float *partials) {
+           const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms, float *partials,
+           bool nv = false, float alpha = 1.0f) {
     CUtensorMap map_w, map_a;
     if (!tc::make_map_sw128(&map_w, w, k / 2, n, 128) || !tc::make_map_sw128(&map_a, a, k / 2, m, p.nt)) {
         set_error("fp4_mma: cuTensorMapEncodeTiled failed (m=%u n=%u k=%u)", m, n, k);
@@ -452,8 +482,11 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(mxf4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err = cudaFuncSetAttribute(mxf4_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)kSmemLimit);
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(mxf4_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kSmemLimit);
     });
     if (attr_err != cudaSuccess) {
         set_error("fp4_mma: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
@@ -463,8 +496,12 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
         set_error("fp4_mma: split-K launch without a workspace");
         return FP4X_EINVAL;
     }
-    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials};
-    mxf4_gemm_kernel<<<dim3(p.m_tiles, p.n_tiles, p.splits), kThreads, p.g.smem, s>>>(map_w, map_a, args);
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials, alpha};
+    const dim3 grid(p.m_tiles, p.n_tiles, p.splits);
+    if (nv)
+        mxf4_gemm_kernel<true><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, args);
+    else
+        mxf4_gemm_kernel<false><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, args);
     if (p.splits > 1) {
         const size_t total = (size_t)(m / terms) * n;
         const uint32_t blocks = (uint32_t)std::min<size_t>((total / 4 + 255) / 256 + 1, 8u * (uint32_t)num_sms());
@@ -503,6 +540,33 @@ extern "C" int fp4_mma_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_
     if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d)) return e;
     const mma::Plan p = mma::plan(m, n, k, false);
     return mma::launch((cudaStream_t)stream, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p, 1, nullptr);
+}
+
+extern "C" size_t fp4_mma_nvf4_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
+    if (m == 0 || n == 0 || k == 0) return 0;
+    return mma::partials_bytes(mma::plan(m, n, k, true, true), m, n, 1);
+}
+
+extern "C" int fp4_mma_nvf4(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                            const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float alpha,
+                            uint16_t *d_bf16, void *workspace, size_t workspace_bytes) {
+    if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d_bf16)) return e;
+    const mma::Plan p = mma::plan(m, n, k, true, true);
+    const size_t need = mma::partials_bytes(p, m, n, 1);
+    if (p.splits > 1)
+        FP4X_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+                     "fp4_mma_nvf4: split-K needs a 16-byte aligned workspace of %zu bytes", need);
+    return mma::launch((cudaStream_t)stream, m, n, k, a, a_scales, w, w_scales, d_bf16, mma::OUT_BF16, p, 1,
+                       static_cast<float *>(workspace), true, alpha);
+}
+
+extern "C" int fp4_mma_nvf4_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
+                                const uint8_t *a_scales, const uint8_t *w, const uint8_t *w_scales, float alpha,
+                                float *d) {
+    if (int e = mma::validate(m, n, k, a, a_scales, w, w_scales, d)) return e;
+    const mma::Plan p = mma::plan(m, n, k, false, true);
+    return mma::launch((cudaStream_t)stream, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p, 1, nullptr, true,
+                       alpha);
 }
 
 extern "C" int fp4_mma_allones(fp4x_stream_t stream, float *out) {

@@ -60,6 +60,54 @@ __device__ __forceinline__ void quant_block_mxfp4(const float (&v)[32], uint4 &p
     sbyte = (uint8_t)e;
 }
 
+// ---- NVFP4: E2M1 with an unsigned-E4M3 scale per 16 values and a per-tensor f32
+// scale g (the reference's kind::mxf4nvf4 / .ue4m3 variant,
+// trackb/FP4_M16N8K64_LAYOUT.md:7; the reference has no quantiser for it).  Rule:
+// s = amax / 6 / g rounded to the nearest UE4M3 (ties to even, saturating at 448,
+// zero for s <= 0), values divided by UE4M3(s) * g and rounded to E2M1 with the
+// reference's tie rule.
+__device__ __forceinline__ float ue4m3_to_f32(uint32_t b) {
+    const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+    return e == 0 ? ldexpf((float)m, -9) : ldexpf((float)(8u + m), (int)e - 10);
+}
+
+__device__ __forceinline__ uint32_t f32_to_ue4m3(float s) {
+    if (!(s > 0.0f)) return 0u;
+    if (s >= 448.0f) return 0x7Eu;
+    if (s < 0.015625f) return (uint32_t)rintf(s * 512.0f);  // subnormal step 2^-9 (8 = smallest normal)
+    const int e = (int)((__float_as_uint(s) >> 23) & 0xFFu) - 127;
+    const float mant = ldexpf(s, -e) - 1.0f;  // exact
+    int E = e + 7, m = (int)rintf(mant * 8.0f);
+    if (m == 8) E += 1, m = 0;
+    if (E > 15 || (E == 15 && m == 7)) return 0x7Eu;
+    return (uint32_t)((E << 3) | m);
+}
+
+// One thread per (row, 16-block).
+__global__ void quant_nvfp4_kernel(uint64_t nblocks, const float *__restrict__ w, uint8_t *__restrict__ packed,
+                                   uint8_t *__restrict__ scales, float g) {
+    const uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    float v[16];
+    const float4 *src = reinterpret_cast<const float4 *>(w + blk * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 f = src[i];
+        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint32_t S = f32_to_ue4m3(__fdiv_rn(__fdiv_rn(amax, 6.0f), g));
+    const float eff = __fmul_rn(ue4m3_to_f32(S), g);
+    uint32_t words[2] = {0, 0};
+    if (eff > 0.0f)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) words[i / 8] |= nearest_code(__fdiv_rn(v[i], eff)) << ((i % 8) * 4);
+    reinterpret_cast<uint2 *>(packed)[blk] = make_uint2(words[0], words[1]);
+    scales[blk] = (uint8_t)S;
+}
+
 // One thread per (row, 32-block).
 __global__ void quant_mxfp4_kernel(uint64_t nblocks, const float *__restrict__ w, uint8_t *__restrict__ packed,
                                    uint8_t *__restrict__ scales) {
@@ -207,6 +255,18 @@ int init_mxfp4_rowmap(cudaStream_t stream, uint64_t seed, float sigma, uint32_t 
 }  // namespace fp4x
 
 using namespace fp4x;
+
+extern "C" int fp4_quantize_nvfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w, uint8_t *packed,
+                                  uint8_t *scales, float global_scale) {
+    FP4X_REQUIRE(w && packed && scales, "fp4_quantize_nvfp4: null pointer");
+    FP4X_REQUIRE(k % 16 == 0 && k > 0 && n > 0, "fp4_quantize_nvfp4: k=%u must be a positive multiple of 16", k);
+    FP4X_REQUIRE(global_scale > 0.0f && global_scale < 3.0e38f, "fp4_quantize_nvfp4: global scale must be positive");
+    FP4X_REQUIRE(aligned16(w) && ((uintptr_t)packed & 7u) == 0, "fp4_quantize_nvfp4: w 16-byte, packed 8-byte aligned");
+    const uint64_t nb = (uint64_t)n * (k / 16);
+    quant::quant_nvfp4_kernel<<<quant::grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(nb, w, packed, scales,
+                                                                                        global_scale);
+    return check_launch("fp4_quantize_nvfp4");
+}
 
 extern "C" int fp4_quantize_mxfp4(fp4x_stream_t stream, uint32_t n, uint32_t k, const float *w, uint8_t *packed,
                                   uint8_t *scales) {

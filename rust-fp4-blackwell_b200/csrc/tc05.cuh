@@ -59,6 +59,12 @@ __host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t n) {
            | ((128u >> 4) << 24);  // M / 16
 }
 
+// Instruction descriptor of kind::mxf4nvf4 with UE4M3 scales per 16 values
+// (NVFP4, scale_vec::4X), otherwise as idesc_mxf4.
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t n) {
+    return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);  // scale format bit 23 = 0: UE4M3
+}
+
 // ---------------------------------------------------------------- TMEM
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -104,6 +110,16 @@ __device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64
         "setp.ne.b32 p, %6, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(id), "r"(tsfa), "r"(tsfb), "r"(accumulate));
+}
+
+// NVFP4 form: 4 UE4M3 scales per row per K=64 (one 32-bit TMEM column), no scale id.
+__device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(tsfa), "r"(tsfb), "r"(accumulate));
 }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread is done.

@@ -54,6 +54,10 @@ SIGNATURES = {
     "fp4_mma_workspace_size": (_sz, [_u32, _u32, _u32]),
     "fp4_mma": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
     "fp4_mma_f32": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "fp4_mma_nvf4_workspace_size": (_sz, [_u32, _u32, _u32]),
+    "fp4_mma_nvf4": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _sz]),
+    "fp4_mma_nvf4_f32": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, C.c_float, _vp]),
+    "fp4_quantize_nvfp4": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp, C.c_float]),
     "fp4_mma_allones": (C.c_int, [_vp, _vp]),
     "llama_rmsnorm": (C.c_int, [_vp, _u32, _f32, _vp, _vp, _vp]),
     "llama_rope": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp]),

@@ -28,6 +28,15 @@ def quantize_mxfp4(w: torch.Tensor):
     return packed, scales
 
 
+def quantize_nvfp4(w: torch.Tensor, global_scale: float = 1.0):
+    """f32 [n][k] -> NVFP4 (packed [n][k/2], UE4M3 scales [n][k/16])."""
+    n, k = w.shape
+    packed = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((n, k // 16), dtype=torch.uint8, device=w.device)
+    check(lib().fp4_quantize_nvfp4(_stream(), n, k, _ptr(w), _ptr(packed), _ptr(scales), global_scale))
+    return packed, scales
+
+
 def quantize_ref(w: torch.Tensor):
     n, k = w.shape
     packed = torch.empty((n, k // 8), dtype=torch.int32, device=w.device)
@@ -100,6 +109,22 @@ def mma(a: torch.Tensor, sa: torch.Tensor, w: torch.Tensor, sw: torch.Tensor, ou
     ws_bytes = lib().fp4_mma_workspace_size(m, n, k)
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=a.device)
     check(lib().fp4_mma(_stream(), m, n, k, _ptr(a), _ptr(sa), _ptr(w), _ptr(sw), _ptr(d), _ptr(ws), ws_bytes))
+    return d
+
+
+def mma_nvf4(a, sa, w, sw, alpha: float = 1.0, out_dtype=torch.bfloat16):
+    """NVFP4 GEMM: d[m][n] = alpha * A W^T, UE4M3 scales per 16 values."""
+    m, n, k = a.shape[0], w.shape[0], a.shape[1] * 2
+    if w.shape[1] * 2 != k or sa.shape != (m, k // 16) or sw.shape != (n, k // 16):
+        raise ValueError("nvf4 mma: operand shapes disagree")
+    d = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    if out_dtype == torch.float32:
+        check(lib().fp4_mma_nvf4_f32(_stream(), m, n, k, _ptr(a), _ptr(sa), _ptr(w), _ptr(sw), alpha, _ptr(d)))
+        return d
+    ws_bytes = lib().fp4_mma_nvf4_workspace_size(m, n, k)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=a.device)
+    check(lib().fp4_mma_nvf4(_stream(), m, n, k, _ptr(a), _ptr(sa), _ptr(w), _ptr(sw), alpha, _ptr(d), _ptr(ws),
+                             ws_bytes))
     return d
 
 
