@@ -227,19 +227,30 @@ def run_config3(args):
     for m in ms:
         for name in names:
             n, k = C3_LINEARS[name]
-            wbytes = n * k // 2 + n * k // 32
+            wbytes = n * k // 2 + n * k // (16 if args.c3_format == "nvf4" else 32)
             copies = max(2, -(-(300 << 20) // wbytes))
-            ws = [ops.init_mxfp4(n, k, seed=100 + i) for i in range(copies)]
-            a, sa = ops.init_mxfp4(m, k, seed=7, sigma=1.0)
+            nv = args.c3_format == "nvf4"
+            if nv:  # NVFP4: one quantised matrix, cloned into distinct copies (L2 rotation)
+                w0 = ops.quantize_nvfp4(ops.fill_normal(n * k, seed=100, sigma=0.02).view(n, k), 1.0 / 4096.0)
+                ws = [(w0[0].clone(), w0[1].clone()) for _ in range(copies)]
+                a, sa = ops.quantize_nvfp4(ops.fill_normal(m * k, seed=7, sigma=1.0).view(m, k), 1.0 / 64.0)
+                wsb = L.fp4_mma_nvf4_workspace_size(m, n, k)
+            else:
+                ws = [ops.init_mxfp4(n, k, seed=100 + i) for i in range(copies)]
+                a, sa = ops.init_mxfp4(m, k, seed=7, sigma=1.0)
+                wsb = L.fp4_mma_workspace_size(m, n, k)
             d = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
-            wsb = L.fp4_mma_workspace_size(m, n, k)
             wsp = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
 
             def call(p, sc):
-                check(L.fp4_mma(s.cuda_stream, m, n, k, a.data_ptr(), sa.data_ptr(), p.data_ptr(), sc.data_ptr(),
-                                d.data_ptr(), wsp.data_ptr(), wsb))
+                if nv:
+                    check(L.fp4_mma_nvf4(s.cuda_stream, m, n, k, a.data_ptr(), sa.data_ptr(), p.data_ptr(),
+                                         sc.data_ptr(), 1.0 / 262144.0, d.data_ptr(), wsp.data_ptr(), wsb))
+                else:
+                    check(L.fp4_mma(s.cuda_stream, m, n, k, a.data_ptr(), sa.data_ptr(), p.data_ptr(), sc.data_ptr(),
+                                    d.data_ptr(), wsp.data_ptr(), wsb))
             with torch.cuda.stream(s):
                 call(*ws[0])
             torch.cuda.synchronize()
@@ -258,7 +269,7 @@ def run_config3(args):
             e1.record(st)
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
-            byts = wbytes + m * k // 2 + m * k // 32 + m * n * 2
+            byts = wbytes + m * k // 2 + m * k // (16 if args.c3_format == "nvf4" else 32) + m * n * 2
             flop = 2.0 * m * n * k
             rows.append({"m": m, "linear": name, "n": n, "k": k, "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
                          "tflops": round(flop / us / 1e6, 1), "split_k": wsb > 0})
@@ -267,9 +278,11 @@ def run_config3(args):
                 tot_us += us
             del ws, g
             torch.cuda.empty_cache()
-    line = {"metric": f"fp4_mma config3: TinyLlama linears at M={ms[-1]} tokens", "value": tot_flop / tot_us / 1e6,
+    fmt = "NVFP4 " if args.c3_format == "nvf4" else ""
+    line = {"metric": f"fp4_mma {fmt}config3: TinyLlama linears at M={ms[-1]} tokens", "value": tot_flop / tot_us / 1e6,
             "unit": "TFLOP/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
-            "dtype": "e2m1 x e2m1 (E8M0 block-32 scales), fp32 accumulate, bf16 out",
+            "dtype": ("e2m1 x e2m1 (UE4M3 block-16 scales), fp32 accumulate, bf16 out" if fmt else
+                      "e2m1 x e2m1 (E8M0 block-32 scales), fp32 accumulate, bf16 out"),
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations -> MXFP4)",
             "config": {"workload": "config3", "tokens": ms, "linears": names,
                        "l2": "rotated weight copies > 300 MB per graph"},
@@ -544,6 +557,8 @@ def main():
     ap.add_argument("--c2-ctx", default="512,2048,8192,32768")
     ap.add_argument("--c2-batch", default="1,8,64")
     ap.add_argument("--c3-linears", default=",".join(C3_LINEARS))
+    ap.add_argument("--c3-format", default="mxf4", choices=["mxf4", "nvf4"],
+                    help="operand format of the config-3 sweep (NVFP4: UE4M3 scales per 16)")
     ap.add_argument("--batch", type=int, default=0, help="batched decode of this many sequences instead")
     ap.add_argument("--batch-model", default="llama8b", choices=["llama8b", "tinyllama"])
     ap.add_argument("--batch-ctx", type=int, default=4096)
