@@ -38,10 +38,12 @@
 
 struct fp4x_llama_batch {
     fp4x_llama_model *m = nullptr;
-    uint32_t rows = 0;     // sequences (decode rows) = rows per prefill pass
+    uint32_t rows = 0;     // rows per pass (prefill tokens per pass; decode rows = seqs)
+    uint32_t seqs = 0;     // sequences, each with its own KV cache (== rows for llama_batch_create)
     uint32_t max_seq = 0;  // positions per sequence cache
+    bool own_kv = true;    // false: the caches are the model's (its one-sequence prefill batch)
     std::vector<void *> allocs;
-    uint16_t *kv = nullptr;  // K [L][rows][max_seq][kvd], then V
+    uint16_t *kv = nullptr;  // K [L][seqs][max_seq][kvd], then V
     float *x = nullptr;      // residual rows [rows][dim]
     float *qkv = nullptr;    // [rows][qd + 2 kvd] (storage row order), kept zero between uses
     float *q = nullptr;      // roped q rows [rows][qd]
@@ -352,7 +354,7 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
     fp4x_llama_model *m = b->m;
     const fp4x_llama_config &c = m->lc;
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
-    const size_t layer_kv = (size_t)b->rows * b->max_seq * kvd;
+    const size_t layer_kv = (size_t)b->seqs * b->max_seq * kvd;
     uint16_t *kbase = b->kv, *vbase = b->kv + (size_t)c.n_layers * layer_kv;
     attn::Params ap{};
     ap.batch = R, ap.n_heads = c.n_heads, ap.n_kv = c.n_kv_heads, ap.seq = 1, ap.max_seq = b->max_seq;
@@ -445,18 +447,22 @@ void destroy(fp4x_llama_batch *b) {
 
 using namespace fp4x;
 
-extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama_batch **out) {
+namespace fp4x {
+namespace batch {
+// rows per pass, seqs caches (kv: the caches, or null to allocate them).
+int create(fp4x_llama_model *m, uint32_t rows, uint32_t seqs, uint16_t *kv, fp4x_llama_batch **out) {
     FP4X_REQUIRE(m && out, "llama_batch_create: null pointer");
-    FP4X_REQUIRE(rows >= 1 && rows <= 256, "llama_batch_create: rows %u not in [1, 256]", rows);
+    FP4X_REQUIRE(rows >= 1 && rows <= 256 && seqs >= 1 && seqs <= rows, "llama_batch_create: rows %u not in [1, 256]",
+                 rows);
     const fp4x_llama_config &c = m->lc;
     FP4X_REQUIRE(c.dim % 64 == 0 && c.ffn % 64 == 0 && (c.n_heads * c.head_dim) % 64 == 0,
                  "llama_batch_create: dim, ffn and n_heads * head_dim must be multiples of 64");
     *out = nullptr;
     fp4x_llama_batch *b = new (std::nothrow) fp4x_llama_batch();
     if (!b) return FP4X_ENOMEM;
-    b->m = m, b->rows = rows, b->max_seq = c.max_seq;
+    b->m = m, b->rows = rows, b->seqs = seqs, b->max_seq = c.max_seq, b->own_kv = kv == nullptr;
     if (const char *e = getenv("FP4X_BATCH_TERMS")) b->terms = atoi(e) == 4 ? 4 : 8;
-    b->len.assign(rows, 0);
+    b->len.assign(seqs, 0);
     const uint32_t hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
     const uint32_t kmax = std::max(std::max(c.dim, c.ffn), qd);
     uint32_t splits = 1, split_len = 0;
@@ -466,10 +472,15 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
         batch::attn_geometry(m, r, c.max_seq, s2, l2);
         b->attn_ws_bytes = std::max(b->attn_ws_bytes, attn::workspace_bytes(r, c.n_heads, hd, s2));
     }
-    int rc = batch::alloc(b, &b->kv, (size_t)2 * c.n_layers * rows * c.max_seq * kvd);
-    if (!rc) rc = cudaMemset(b->kv, 0, (size_t)2 * c.n_layers * rows * c.max_seq * kvd * 2) == cudaSuccess
-                      ? FP4X_OK
-                      : batch::cuda_fail("llama_batch_create: clear KV", cudaGetLastError());
+    int rc = FP4X_OK;
+    if (kv) {
+        b->kv = kv;
+    } else {
+        rc = batch::alloc(b, &b->kv, (size_t)2 * c.n_layers * seqs * c.max_seq * kvd);
+        if (!rc) rc = cudaMemset(b->kv, 0, (size_t)2 * c.n_layers * seqs * c.max_seq * kvd * 2) == cudaSuccess
+                          ? FP4X_OK
+                          : batch::cuda_fail("llama_batch_create: clear KV", cudaGetLastError());
+    }
     if (!rc) rc = batch::alloc(b, &b->x, (size_t)rows * c.dim);
     if (!rc) rc = batch::alloc(b, &b->qkv, (size_t)rows * (qd + 2 * kvd));
     if (!rc) rc = batch::alloc(b, &b->q, (size_t)rows * qd);
@@ -481,21 +492,21 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     if (!rc) rc = batch::alloc(b, &b->act_s, (size_t)rows * b->terms * kmax / 32);
     b->mma_part_bytes = batch::mma_ws_need(m, rows, b->terms);
     if (!rc) rc = batch::alloc(b, &b->mma_part, std::max<size_t>(4, b->mma_part_bytes / 4));
-    if (!rc) rc = batch::alloc(b, &b->dec_tok, rows);
-    if (!rc) rc = batch::alloc(b, &b->dec_pos, rows);
+    if (!rc) rc = batch::alloc(b, &b->dec_tok, seqs);
+    if (!rc) rc = batch::alloc(b, &b->dec_pos, seqs);
     if (!rc) rc = batch::alloc(b, &b->pf_tok, rows);
     if (!rc) rc = batch::alloc(b, &b->pf_pos, rows);
     if (!rc) rc = batch::alloc(b, &b->pf_cache, rows);
     if (!rc) rc = batch::alloc(b, &b->prompt, c.max_seq);
-    if (!rc) rc = batch::alloc(b, &b->ids, (size_t)rows * c.max_seq);
+    if (!rc) rc = batch::alloc(b, &b->ids, (size_t)seqs * c.max_seq);
     if (!rc && m->cfg.tp_size > 1) {
         rc = batch::alloc(b, &b->part, (size_t)rows * c.dim);
         if (!rc) rc = tp::row_create(&b->rx, m->cfg.tp_rank, m->cfg.tp_size, (size_t)rows * c.dim);
     }
     if (!rc && (cudaMemset(b->qkv, 0, (size_t)rows * (qd + 2 * kvd) * 4) != cudaSuccess ||
                 cudaMemset(b->gu, 0, (size_t)rows * 2 * c.ffn * 4) != cudaSuccess ||
-                cudaMemset(b->dec_tok, 0, rows * 4) != cudaSuccess || cudaMemset(b->dec_pos, 0, rows * 4) != cudaSuccess ||
-                cudaMemset(b->ids, 0, (size_t)rows * c.max_seq * 4) != cudaSuccess))
+                cudaMemset(b->dec_tok, 0, seqs * 4) != cudaSuccess || cudaMemset(b->dec_pos, 0, seqs * 4) != cudaSuccess ||
+                cudaMemset(b->ids, 0, (size_t)seqs * c.max_seq * 4) != cudaSuccess))
         rc = batch::cuda_fail("llama_batch_create: clear", cudaGetLastError());
     if (!rc && cudaStreamCreateWithFlags(&b->cap_stream, cudaStreamNonBlocking) != cudaSuccess)
         rc = batch::cuda_fail("llama_batch_create: stream", cudaGetLastError());
@@ -508,6 +519,13 @@ extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama
     return FP4X_OK;
 }
 
+}  // namespace batch
+}  // namespace fp4x
+
+extern "C" int llama_batch_create(fp4x_llama_model *m, uint32_t rows, fp4x_llama_batch **out) {
+    return batch::create(m, rows, rows, nullptr, out);
+}
+
 extern "C" int llama_batch_destroy(fp4x_llama_batch *b) {
     batch::destroy(b);
     return FP4X_OK;
@@ -517,7 +535,7 @@ extern "C" int llama_batch_prefill(fp4x_llama_batch *b, fp4x_stream_t stream, ui
                                    uint32_t n) {
     FP4X_REQUIRE(b && tokens, "llama_batch_prefill: null pointer");
     FP4X_REQUIRE(!b->rx || b->rx->connected, "llama_batch_prefill: tensor-parallel batch not connected");
-    FP4X_REQUIRE(seq < b->rows, "llama_batch_prefill: sequence %u of %u", seq, b->rows);
+    FP4X_REQUIRE(seq < b->seqs, "llama_batch_prefill: sequence %u of %u", seq, b->seqs);
     FP4X_REQUIRE(n >= 1 && b->len[seq] + n < b->max_seq, "llama_batch_prefill: %u tokens after %u exceed max_seq %u",
                  n, b->len[seq], b->max_seq);
     const uint32_t vocab = b->m->cfg.vocab;
@@ -545,7 +563,7 @@ extern "C" int llama_batch_prefill(fp4x_llama_batch *b, fp4x_stream_t stream, ui
 extern "C" int llama_batch_set_length(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t seq, uint32_t len,
                                       uint32_t next_token) {
     FP4X_REQUIRE(b, "llama_batch_set_length: null pointer");
-    FP4X_REQUIRE(seq < b->rows && len < b->max_seq && next_token < b->m->cfg.vocab,
+    FP4X_REQUIRE(seq < b->seqs && len < b->max_seq && next_token < b->m->cfg.vocab,
                  "llama_batch_set_length: sequence %u, length %u, token %u out of range", seq, len, next_token);
     cudaStream_t st = (cudaStream_t)stream;
     const uint32_t v[2] = {next_token, len};
@@ -561,20 +579,21 @@ extern "C" int llama_batch_set_length(fp4x_llama_batch *b, fp4x_stream_t stream,
 extern "C" int llama_batch_decode(fp4x_llama_batch *b, fp4x_stream_t stream, uint32_t n_steps) {
     FP4X_REQUIRE(b, "llama_batch_decode: null pointer");
     FP4X_REQUIRE(!b->rx || b->rx->connected, "llama_batch_decode: tensor-parallel batch not connected");
-    for (uint32_t s = 0; s < b->rows; ++s)
+    FP4X_REQUIRE(b->seqs == b->rows, "llama_batch_decode: a prefill-only batch");
+    for (uint32_t s = 0; s < b->seqs; ++s)
         FP4X_REQUIRE(b->len[s] + n_steps < b->max_seq, "llama_batch_decode: sequence %u at %u + %u steps exceeds %u", s,
                      b->len[s], n_steps, b->max_seq);
     FP4X_TRY(batch::build_graph(b));
     cudaStream_t st = (cudaStream_t)stream;
     for (uint32_t i = 0; i < n_steps; ++i)
         if (cudaGraphLaunch(b->exec, st) != cudaSuccess) return batch::cuda_fail("llama_batch_decode", cudaGetLastError());
-    for (uint32_t s = 0; s < b->rows; ++s) b->len[s] += n_steps;
+    for (uint32_t s = 0; s < b->seqs; ++s) b->len[s] += n_steps;
     b->last_rows = b->rows;
     return FP4X_OK;
 }
 
 extern "C" int llama_batch_tokens(fp4x_llama_batch *b, uint32_t seq, uint32_t *out, uint32_t n, uint32_t *len_out) {
-    FP4X_REQUIRE(b && seq < (b ? b->rows : 0), "llama_batch_tokens: bad sequence");
+    FP4X_REQUIRE(b && seq < (b ? b->seqs : 0), "llama_batch_tokens: bad sequence");
     const uint32_t len = b->len[seq] + 1;  // positions 0..len-1 hold tokens (the last one not yet consumed)
     if (len_out) *len_out = len;
     if (!out || n == 0) return FP4X_OK;
@@ -598,7 +617,7 @@ extern "C" int llama_batch_logits(fp4x_llama_batch *b, float *out, uint32_t *row
 extern "C" size_t llama_batch_kv_bytes(const fp4x_llama_batch *b) {
     if (!b) return 0;
     const fp4x_llama_config &c = b->m->lc;
-    return (size_t)2 * c.n_layers * b->rows * b->max_seq * c.n_kv_heads * c.head_dim * 2;
+    return (size_t)2 * c.n_layers * b->seqs * b->max_seq * c.n_kv_heads * c.head_dim * 2;
 }
 
 extern "C" int llama_batch_tp_handle(fp4x_llama_batch *b, void *handle_out) {
@@ -612,3 +631,29 @@ extern "C" int llama_batch_tp_connect(fp4x_llama_batch *b, const void *handles) 
     FP4X_REQUIRE(b->rx, "llama_batch_tp_connect: the model is not tensor parallel");
     return tp::row_connect(b->rx, handles);
 }
+
+namespace fp4x {
+namespace batch {
+
+// Hand-over from a batched prompt prefill to the model's device-resident loop:
+// the first generated token is the next input at position n_prompt.
+__global__ void finish_prefill_kernel(const uint32_t *first, uint32_t *state, uint32_t *out, uint32_t n_prompt) {
+    const uint32_t g = first[0];
+    state[0] = g, state[1] = n_prompt, state[2] = g;
+    out[0] = g;
+}
+
+// Prompt prefill of the model (batch 1) through the batched engine: passes of up to
+// 64 prompt tokens, K/V written into the model's own cache (a one-sequence batch
+// cache has its [layer][max_seq][kvd] layout).  Replaces the token-at-a-time
+// prefill of llama_run/src/main.rs:550-556.
+int model_prefill(fp4x_llama_model *m, cudaStream_t st, const uint32_t *prompt, uint32_t n) {
+    if (!m->pf) FP4X_TRY(create(m, std::min(64u, m->cfg.max_seq), 1, m->kv, &m->pf));
+    m->pf->len[0] = 0;
+    FP4X_TRY(llama_batch_prefill(m->pf, (fp4x_stream_t)st, 0, prompt, n));
+    finish_prefill_kernel<<<1, 1, 0, st>>>(m->pf->dec_tok, m->state, m->out, n);
+    return check_launch("llama_generate: prefill hand-over");
+}
+
+}  // namespace batch
+}  // namespace fp4x

@@ -80,6 +80,7 @@ struct fp4x_llama_model {
     uint16_t *kv = nullptr;        // K [L][max_seq][kvd] then V [L][max_seq][kvd]
     fp4x::persist::Engine *pe = nullptr;  // persistent decode kernel (null: unsupported shape)
     fp4x::ptc::Engine *pt = nullptr;      // tensor-core persistent decode kernel (null: unsupported)
+    fp4x_llama_batch *pf = nullptr;        // prompt prefill through the batched engine (created on first use)
     int path = 0;                  // 0: CUDA graph of fused kernels, 1: persistent kernel (CUDA-core
                                    // MXFP4 decode), 2: persistent kernel on tcgen05 MMAs
     int64_t hpos = -1;             // host view of the device-resident position (-1: unknown)
@@ -88,6 +89,10 @@ struct fp4x_llama_model {
 };
 
 namespace fp4x {
+namespace batch {
+void destroy(fp4x_llama_batch *b);                                                        // batch.cu
+int model_prefill(fp4x_llama_model *m, cudaStream_t st, const uint32_t *prompt, uint32_t n);  // batch.cu
+}  // namespace batch
 namespace engine {
 
 __device__ __forceinline__ void argmax_merge(float &bv, uint32_t &bi, float ov, uint32_t oi) {
@@ -491,6 +496,7 @@ extern "C" int llama_model_destroy(fp4x_llama_model *m) {
         cudaStreamSynchronize(m->cap_stream);
         cudaStreamDestroy(m->cap_stream);
     }
+    batch::destroy(m->pf);
     persist::destroy(m->pe);
     ptc::destroy(m->pt);
     tp::destroy(m->xc);
@@ -564,9 +570,17 @@ extern "C" int llama_generate(fp4x_llama_model *m, fp4x_stream_t stream, const u
     FP4X_CUDA(cudaEventCreate(&e1));
     FP4X_CUDA(cudaEventCreate(&e2));
     FP4X_CUDA(cudaEventRecord(e0, st));
-    // prefill = the same one-token path over the prompt (llama_run:550-556); the
+    // prefill: the prompt in multi-token passes of the batched engine (written into
+    // this model's KV cache), or -- under tensor parallelism, or FP4X_PREFILL=serial --
+    // the one-token decode path over the prompt as llama_run:550-556; either way the
     // last prompt position yields the first generated token
-    FP4X_TRY(run_tokens(m, st, n_prompt));
+    const char *pfe = getenv("FP4X_PREFILL");
+    if (!m->xc && !(pfe && strcmp(pfe, "serial") == 0)) {
+        FP4X_TRY(batch::model_prefill(m, st, prompt, n_prompt));
+        m->hpos = n_prompt;
+    } else {
+        FP4X_TRY(run_tokens(m, st, n_prompt));
+    }
     FP4X_CUDA(cudaEventRecord(e1, st));
     FP4X_TRY(run_tokens(m, st, n_gen - 1));
     FP4X_CUDA(cudaEventRecord(e2, st));

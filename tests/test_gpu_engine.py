@@ -214,3 +214,24 @@ def test_engine_long_context_split_attention(cfg):
                 worst = max(worst, compare_logits(gl, rl))
     ref.close()
     print(f"long context: worst logits rel err {worst:.3e}")
+
+
+@pytest.mark.parametrize("path", ["graph", "tensor"])
+def test_generate_batched_prefill_matches_oracle_long_prompt(path, monkeypatch):
+    """llama_generate prefills the prompt through the batched engine (passes of 64
+    tokens into the model's KV cache); a 150-token prompt spans three passes.  The
+    generated tokens equal the oracle's, and the one-token prefill
+    (FP4X_PREFILL=serial) gives the same ids."""
+    cfg = dict(TINY, max_seq=200)
+    prompt = oracle.uniform_ids(31, cfg["vocab"], 150)
+    ref = oracle.Model(cfg)
+    want = ref.generate(prompt, 12)
+    ref.close()
+    with engine.Model(cfg) as m:
+        m.set_path(path)
+        got, pre_ms, _ = m.generate(prompt, 12)
+        monkeypatch.setenv("FP4X_PREFILL", "serial")
+        m.reset()
+        got_serial, _, _ = m.generate(prompt, 12)
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal(got_serial, want)
