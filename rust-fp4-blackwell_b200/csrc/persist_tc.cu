@@ -451,14 +451,54 @@ __device__ void decompose8(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb,
     }
 }
 
-// RMSNorm + decomposition in registers: thread i owns values [8i, 8i+8) (and
-// [8(i+kCons), ...) when dim > 8 * kCons).  xn = (src * rms) * w
+// Half-word form: 4 values per thread (thread j of a 32-block owns values
+// [4j, 4j + 4): the 8 threads of a block in adjacent lanes, j even = low half of
+// word j / 2).  Same arithmetic per value as term_words8 (same bits); the term
+// chain is half as long and twice as many threads share the vector.
+__device__ __forceinline__ void decompose_half8(float (&x)[4], uint32_t b, uint32_t j, bool valid, uint8_t *B,
+                                                uint8_t *sfb) {
+    float a = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+    const uint32_t bits = __float_as_uint(a);
+    int e1 = (int)((bits >> 23) & 0xFFu) - 127;
+    e1 = (bits & 0x7FFFFFu) <= 0x400000u ? e1 - 2 : e1 - 1;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const int e = term_exp(e1, t);
+        const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+        const float s = __uint_as_float((uint32_t)(127 + e) << 23);
+        uint32_t h;  // 4 nibbles in the low 16 bits
+        asm("{\n\t.reg .b8 q0, q1, z;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 z, %5, %5;\n\t"
+            "mov.b32 %0, {q0, q1, z, z};\n\t}"
+            : "=r"(h)
+            : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv), "f"(0.0f));
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const uint32_t hv = e2m1x2_to_f16x2((h >> (8 * q)) & 0xFFu);
+            const __half2 d = *reinterpret_cast<const __half2 *>(&hv);
+            x[2 * q] = fmaf(-__low2float(d), s, x[2 * q]);
+            x[2 * q + 1] = fmaf(-__high2float(d), s, x[2 * q + 1]);
+        }
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, h, 1);
+        if (valid && (j & 1) == 0) *reinterpret_cast<uint32_t *>(B + b * 128 + t * 16 + (j >> 1) * 4) = h | (other << 16);
+    }
+    if (valid && j == 0)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) sfb[(b >> 2) * 128 + t * 16 + (b & 3)] = (uint8_t)(term_exp(e1, t) + 127);
+}
+
+// RMSNorm + decomposition in registers: thread i owns values [4i, 4i+4) (and
+// [4(i+kCons), ...) when dim > 4 * kCons).  xn = (src * rms) * w
 // (llama_run:79-116), src = X (MODE 0), X + Y (1) or the bf16 embedding row (2;
 // CTA 0 writes it to X).  With `decompose` false only the CTA-0 embedding copy runs.
 template <int MODE>
 __device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, bool decompose) {
     const Params &p = *c.p;
-    constexpr int R = 2;  // dim <= 16 * kCons
     const uint32_t nw = p.dim / 8, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (!decompose) {
         if (MODE == 2 && blockIdx.x == 0)
@@ -472,41 +512,35 @@ __device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, boo
             }
         return;
     }
-    float x[R][8];
+    // thread i owns the 4-value groups i, i + kCons, ... (values [4g, 4g + 4))
+    constexpr int R4 = 4;  // dim <= 16 * kCons
+    const uint32_t ng = p.dim / 4;
+    float x[R4][4], g[R4][4];
     float ss = 0.0f;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
+    for (int r = 0; r < R4; ++r) {
         const uint32_t i = threadIdx.x + r * kCons;
-        if (i < nw) {
-            if (MODE == 2) {
-                const uint4 q = *reinterpret_cast<const uint4 *>(erow + 8 * i);
-                const uint32_t u[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    x[r][2 * j] = __uint_as_float(u[j] << 16);
-                    x[r][2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
-                }
-                if (blockIdx.x == 0) {
-                    *reinterpret_cast<float4 *>(p.X + 8 * i) = make_float4(x[r][0], x[r][1], x[r][2], x[r][3]);
-                    *reinterpret_cast<float4 *>(p.X + 8 * i + 4) = make_float4(x[r][4], x[r][5], x[r][6], x[r][7]);
-                }
+        for (int j = 0; j < 4; ++j) x[r][j] = 0.0f, g[r][j] = 0.0f;
+        if (i < ng) {
+            float4 v;
+            if (MODE == 2) {
+                const uint2 q = *reinterpret_cast<const uint2 *>(erow + 4 * i);
+                v = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                                __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
+                if (blockIdx.x == 0) *reinterpret_cast<float4 *>(p.X + 4 * i) = v;
             } else {
-                const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(p.X + 8 * i));
-                const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(p.X + 8 * i + 4));
-                x[r][0] = a0.x, x[r][1] = a0.y, x[r][2] = a0.z, x[r][3] = a0.w;
-                x[r][4] = a1.x, x[r][5] = a1.y, x[r][6] = a1.z, x[r][7] = a1.w;
+                v = __ldcg(reinterpret_cast<const float4 *>(p.X + 4 * i));
                 if (MODE == 1) {
-                    const float4 y0 = __ldcg(reinterpret_cast<const float4 *>(p.Y + 8 * i));
-                    const float4 y1 = __ldcg(reinterpret_cast<const float4 *>(p.Y + 8 * i + 4));
-                    x[r][0] += y0.x, x[r][1] += y0.y, x[r][2] += y0.z, x[r][3] += y0.w;
-                    x[r][4] += y1.x, x[r][5] += y1.y, x[r][6] += y1.z, x[r][7] += y1.w;
+                    const float4 y = __ldcg(reinterpret_cast<const float4 *>(p.Y + 4 * i));
+                    v.x += y.x, v.y += y.y, v.z += y.z, v.w += y.w;
                 }
             }
+            const float4 gw = __ldg(reinterpret_cast<const float4 *>(w + 4 * i));
+            x[r][0] = v.x, x[r][1] = v.y, x[r][2] = v.z, x[r][3] = v.w;
+            g[r][0] = gw.x, g[r][1] = gw.y, g[r][2] = gw.z, g[r][3] = gw.w;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ss += x[r][j] * x[r][j];
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) x[r][j] = 0.0f;
+            for (int j = 0; j < 4; ++j) ss += x[r][j] * x[r][j];
         }
     }
     ss = warp_sum(ss);
@@ -518,18 +552,13 @@ __device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, boo
     const float rms = 1.0f / sqrtf(tot / (float)p.dim + p.eps);
     uint8_t *B = c.smem + c.L.bx, *sfb = c.smem + c.L.sfbx;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
+    for (int r = 0; r < R4; ++r) {
         const uint32_t i = threadIdx.x + r * kCons;
-        if (i - lane >= nw) break;  // warp-uniform
-        const bool valid = i < nw;
-        if (valid) {
-            const float4 g0 = __ldg(reinterpret_cast<const float4 *>(w + 8 * i));
-            const float4 g1 = __ldg(reinterpret_cast<const float4 *>(w + 8 * i + 4));
-            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        if (i - lane >= ng) break;  // warp-uniform
+        const bool valid = i < ng;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) x[r][j] = x[r][j] * rms * g[j];
-        }
-        decompose_word8(x[r], i >> 2, i & 3, valid, B, sfb, false);
+        for (int j = 0; j < 4; ++j) x[r][j] = x[r][j] * rms * g[r][j];
+        decompose_half8(x[r], i >> 3, i & 7, valid, B, sfb);
     }
 }
 
