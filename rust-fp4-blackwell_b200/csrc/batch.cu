@@ -53,9 +53,12 @@ struct fp4x_llama_batch {
     float *attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
     uint32_t terms = 8;      // MXFP4 terms per activation row (8, or 4 on request)
-    uint8_t *act = nullptr, *act_s = nullptr;  // term rows [terms rows][kmax / 2], [terms rows][kmax / 32]
+    uint8_t *act = nullptr;    // term rows [terms rows][kmax / 2]
+    uint8_t *act_s = nullptr;  // their E8M0 scales, as the atom image of the GEMM they feed
     float *mma_part = nullptr;  // split-K partials
     size_t mma_part_bytes = 0;
+    // weight scales as the GEMM's 512-byte atom images (per layer: qkv, o, gu, down; then lm_head)
+    std::vector<uint8_t *> wimg;
     uint32_t *dec_tok = nullptr, *dec_pos = nullptr;            // per sequence: next token, its position
     uint32_t *pf_tok = nullptr, *pf_pos = nullptr, *pf_cache = nullptr;  // prefill rows
     uint32_t *prompt = nullptr;  // staging for prefill tokens [max_seq]
@@ -131,7 +134,8 @@ template <int SRC>
 __global__ void __launch_bounds__(kThreads) rows_decompose_kernel(uint32_t K, const float *src, float *x_out,
                                                                   const uint16_t *embed, const uint32_t *tok,
                                                                   const float *norm_w, float eps, uint8_t *act,
-                                                                  uint8_t *act_s, uint32_t row0, uint32_t terms) {
+                                                                  uint8_t *act_s, uint32_t row0, uint32_t terms,
+                                                                  uint32_t img_nt) {
     __shared__ float red[kThreads / 32];
     const uint32_t r = blockIdx.x, rs = row0 + r;  // output row, source row
     const uint32_t nw = K / 8, i = blockIdx.y * kThreads + threadIdx.x;
@@ -175,13 +179,14 @@ __global__ void __launch_bounds__(kThreads) rows_decompose_kernel(uint32_t K, co
     uint32_t words[8];
     const int e1 = ptc::term_words8(x, words);  // every lane of the warp takes part
     if (!valid) return;
-    const size_t row_bytes = K / 2, row_scales = K / 32;
+    const size_t row_bytes = K / 2;
 #pragma unroll
     for (uint32_t t = 0; t < kMaxTerms; ++t) {
         if (t >= terms) break;
         const size_t tr = (size_t)r * terms + t;
         *reinterpret_cast<uint32_t *>(act + tr * row_bytes + 4 * i) = words[t];
-        if ((i & 3) == 0) act_s[tr * row_scales + i / 4] = (uint8_t)(ptc::term_exp(e1, (int)t) + 127);
+        if ((i & 3) == 0)
+            act_s[mma::scale_image_offset((uint32_t)tr, i / 4, K, img_nt)] = (uint8_t)(ptc::term_exp(e1, (int)t) + 127);
     }
 }
 
@@ -300,8 +305,9 @@ int alloc(fp4x_llama_batch *b, T **p, size_t count) {
     return FP4X_OK;
 }
 
-// Term rows = terms x R; out[R][n] = (or +=) the sums.
-int linear(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const QMat &w, float *out, bool accumulate) {
+// Term rows = terms x R; out[R][n] = (or +=) the sums.  img: w's scale atom image.
+int linear(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const QMat &w, const uint8_t *img, float *out,
+           bool accumulate) {
     const uint32_t m = R * b->terms;
     const mma::Plan p = mma::plan(m, w.n, w.k);
     if (mma::partials_bytes(p, m, w.n, b->terms) > b->mma_part_bytes) {
@@ -309,7 +315,7 @@ int linear(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const QMat &w, floa
         return FP4X_EINVAL;
     }
     return mma::launch(st, m, w.n, w.k, b->act, b->act_s, w.w, w.s, out, accumulate ? mma::OUT_ADD_F32 : mma::OUT_F32,
-                       p, b->terms, b->mma_part);
+                       p, b->terms, b->mma_part, false, 1.0f, b->act_s, img);
 }
 
 // Largest split-K scratch a pass of up to `rows` rows needs over the model's linears.
@@ -326,12 +332,16 @@ size_t mma_ws_need(const fp4x_llama_model *m, uint32_t rows, uint32_t terms) {
     return part;
 }
 
+// Token-tile rows of the GEMM fed by R rows of terms (the plan's tile width).
+inline uint32_t act_tile_rows(uint32_t m) { return m >= 256 ? 256 : (m + 7) / 8 * 8; }
+
 template <int SRC>
 int decompose(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, uint32_t K, const float *src, float *x_out,
               const uint32_t *tok, const float *norm_w, uint32_t row0 = 0) {
     const uint32_t chunks = (K / 8 + kThreads - 1) / kThreads;
-    rows_decompose_kernel<SRC><<<dim3(R, chunks), kThreads, 0, st>>>(K, src, x_out, b->m->embed, tok, norm_w,
-                                                                      b->m->lc.eps, b->act, b->act_s, row0, b->terms);
+    rows_decompose_kernel<SRC><<<dim3(R, chunks), kThreads, 0, st>>>(
+        K, src, x_out, b->m->embed, tok, norm_w, b->m->lc.eps, b->act, b->act_s, row0, b->terms,
+        act_tile_rows(R * b->terms));
     return check_launch("llama_batch: decompose");
 }
 
@@ -372,7 +382,8 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
             FP4X_TRY(decompose<SRC_EMBED>(b, st, R, c.dim, nullptr, b->x, tok, L.attn_norm));
         else
             FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.attn_norm));
-        FP4X_TRY(linear(b, st, R, L.qkv, b->qkv, false));
+        const uint8_t *const *wi = b->wimg.data() + 4 * l;
+        FP4X_TRY(linear(b, st, R, L.qkv, wi[0], b->qkv, false));
         rows_rope_append_kernel<<<dim3(R, (qd + 3 * kvd + 2 * kThreads - 1) / (2 * kThreads)), kThreads, 0, st>>>(qd, kvd, hd, b->qkv, b->q, kc, vc, pos, cache, b->max_seq,
                                                         m->cos_t, m->sin_t);
         FP4X_TRY(check_launch("llama_batch: rope"));
@@ -380,25 +391,25 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
         FP4X_TRY(attn::launch_engine(st, ap, hd, false));
         FP4X_TRY(decompose<SRC_PLAIN>(b, st, R, qd, b->att, nullptr, nullptr, nullptr));
         if (b->rx) {  // row-parallel O: local partial, then the cross-rank sum into the residual
-            FP4X_TRY(linear(b, st, R, L.o, b->part, false));
+            FP4X_TRY(linear(b, st, R, L.o, wi[1], b->part, false));
             FP4X_TRY(tp::rows_allreduce_add(st, b->rx, b->part, b->x, (size_t)R * c.dim));
         } else {
-            FP4X_TRY(linear(b, st, R, L.o, b->x, true));
+            FP4X_TRY(linear(b, st, R, L.o, wi[1], b->x, true));
         }
         FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.ffn_norm));
-        FP4X_TRY(linear(b, st, R, L.gu, b->gu, false));
+        FP4X_TRY(linear(b, st, R, L.gu, wi[2], b->gu, false));
         FP4X_TRY(decompose<SRC_SWIGLU>(b, st, R, c.ffn, b->gu, nullptr, nullptr, nullptr));
         if (b->rx) {  // row-parallel down
-            FP4X_TRY(linear(b, st, R, L.down, b->part, false));
+            FP4X_TRY(linear(b, st, R, L.down, wi[3], b->part, false));
             FP4X_TRY(tp::rows_allreduce_add(st, b->rx, b->part, b->x, (size_t)R * c.dim));
         } else {
-            FP4X_TRY(linear(b, st, R, L.down, b->x, true));
+            FP4X_TRY(linear(b, st, R, L.down, wi[3], b->x, true));
         }
     }
     const uint32_t RL = R - lm0;
     if (RL == 0) return FP4X_OK;  // no logits wanted (a prompt chunk before the last)
     FP4X_TRY(decompose<SRC_NORM>(b, st, RL, c.dim, b->x, nullptr, nullptr, m->final_norm, lm0));
-    FP4X_TRY(linear(b, st, RL, m->lm_head, b->logits, false));
+    FP4X_TRY(linear(b, st, RL, m->lm_head, b->wimg[4 * c.n_layers], b->logits, false));
     b->last_rows = RL;
     return FP4X_OK;
 }
@@ -489,7 +500,34 @@ int create(fp4x_llama_model *m, uint32_t rows, uint32_t seqs, uint16_t *kv, fp4x
     if (!rc) rc = batch::alloc(b, &b->logits, (size_t)rows * c.vocab);
     if (!rc) rc = batch::alloc(b, &b->attn_ws, std::max<size_t>(16, b->attn_ws_bytes / 4));
     if (!rc) rc = batch::alloc(b, &b->act, (size_t)rows * b->terms * kmax / 2);
-    if (!rc) rc = batch::alloc(b, &b->act_s, (size_t)rows * b->terms * kmax / 32);
+    size_t act_img = 0;  // the largest activation scale image any pass of <= rows rows writes
+    for (uint32_t r = 1; r <= rows; ++r)
+        act_img = std::max(act_img, mma::scale_image_bytes(r * b->terms, kmax, batch::act_tile_rows(r * b->terms)));
+    if (!rc) rc = batch::alloc(b, &b->act_s, act_img);
+    if (!rc && cudaMemset(b->act_s, 0, act_img) != cudaSuccess)  // only finite E8M0 bytes are ever written
+        rc = batch::cuda_fail("llama_batch_create: clear", cudaGetLastError());
+    auto image = [&](const QMat &w) {
+        uint8_t *img = nullptr;
+        const size_t bytes = mma::scale_image_bytes(w.n, w.k, 128);
+        int e = batch::alloc(b, &img, bytes);
+        if (!e && cudaMemset(img, 0, bytes) != cudaSuccess)  // blocks past k in a partial last stage stay 0
+            e = batch::cuda_fail("llama_batch_create: clear", cudaGetLastError());
+        if (!e) {
+            mma::scale_image_kernel<<<(unsigned)std::min<size_t>((bytes + 255) / 256, 8192), 256>>>(w.s, w.n, w.k, 128,
+                                                                                                   img);
+            e = check_launch("llama_batch_create: scale image");
+        }
+        b->wimg.push_back(img);
+        return e;
+    };
+    for (uint32_t l = 0; l < c.n_layers && !rc; ++l) {
+        const LayerW &L = m->layers[l];
+        rc = image(L.qkv);
+        if (!rc) rc = image(L.o);
+        if (!rc) rc = image(L.gu);
+        if (!rc) rc = image(L.down);
+    }
+    if (!rc) rc = image(m->lm_head);
     b->mma_part_bytes = batch::mma_ws_need(m, rows, b->terms);
     if (!rc) rc = batch::alloc(b, &b->mma_part, std::max<size_t>(4, b->mma_part_bytes / 4));
     if (!rc) rc = batch::alloc(b, &b->dec_tok, seqs);

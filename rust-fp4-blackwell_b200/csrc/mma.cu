@@ -99,7 +99,36 @@ struct Args {
     uint32_t splits;            // K splits (blockIdx.z); > 1: partial sums to ws, added by splitk_reduce_kernel
     float *ws;                  // [splits][m / terms][n] partial sums
     float alpha;                // output multiplier (NVFP4 per-tensor scales; 1 for MXFP4)
+    // MXFP4 only: the scales already arranged as the kernel's 512-byte atoms
+    // (scale_image_bytes layouts), loaded per stage by one bulk copy each instead of
+    // gathered from sa / sw; both null = gather
+    const uint8_t *sa_img, *sw_img;
 };
+
+// Scale-atom image of a [rows][k/32] E8M0 matrix cut into tiles of `tile_rows`
+// rows (128: weights; nt: tokens): [tile][stage of 256 k][tile_rows/128][2][512 B],
+// atom h of a stage holding k-blocks 8 stage + 4h + j of row r at byte
+// 16 (r % 32) + 4 (r / 32) + j (rows / blocks outside the matrix are 0).
+__host__ __device__ inline size_t scale_image_bytes(uint32_t rows, uint32_t k, uint32_t tile_rows) {
+    const uint32_t tiles = (rows + tile_rows - 1) / tile_rows, kst = (k + kStageK - 1) / kStageK;
+    return (size_t)tiles * kst * ((tile_rows + 127) / 128) * 2 * 512;
+}
+__host__ __device__ inline size_t scale_image_offset(uint32_t row, uint32_t kb, uint32_t k, uint32_t tile_rows) {
+    const uint32_t kst = (k + kStageK - 1) / kStageK, qn = (tile_rows + 127) / 128;
+    const uint32_t tile = row / tile_rows, rr = row % tile_rows, q = rr / 128, r = rr % 128;
+    const uint32_t stage = kb / 8, h = (kb % 8) / 4, j = kb % 4;
+    return ((((size_t)tile * kst + stage) * qn + q) * 2 + h) * 512 + 16 * (r % 32) + 4 * (r / 32) + j;
+}
+
+__global__ void scale_image_kernel(const uint8_t *__restrict__ s, uint32_t rows, uint32_t k, uint32_t tile_rows,
+                                   uint8_t *__restrict__ img) {
+    const uint32_t kbt = k / 32, tiles = (rows + tile_rows - 1) / tile_rows;
+    const size_t total = (size_t)tiles * tile_rows * kbt;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t row = (uint32_t)(i / kbt), kb = (uint32_t)(i % kbt);
+        img[scale_image_offset(row, kb, k, tile_rows)] = row < rows ? s[(size_t)row * kbt + kb] : (uint8_t)0;
+    }
+}
 
 __device__ __forceinline__ void emit(const Args &a, uint32_t tok, uint32_t row, float v) {
     const size_t o = (size_t)tok * a.n + row;
@@ -228,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / (NV ? 16 : 32);
     const uint32_t s0 = blockIdx.z * a.kps, s1 = min(kst, s0 + a.kps);
     const uint32_t nst = s1 > s0 ? s1 - s0 : 0;
+    const bool pre = !NV && a.sa_img != nullptr;  // scale atoms arrive by bulk copy with the tiles
     // CTAs walk their K stages in rotated order (start = weight tile index mod
     // stages) so that concurrent CTAs do not all read the same activation lines
     // of L2 at the same moment.
@@ -262,10 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t slot = i % S;
                 if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
                 uint8_t *st = smem + slot * G.stage_bytes;
-                mbar_arrive_expect_tx(&full_t[slot], kTileA + a.nt * 128);
-                const int32_t kx = (int32_t)(stage_of(i) * 128);
+                const uint32_t sw_bytes = G.ak * 512, sa_bytes = G.sfb_atoms * G.ak * 512;
+                mbar_arrive_expect_tx(&full_t[slot], kTileA + a.nt * 128 + (pre ? sw_bytes + sa_bytes : 0u));
+                const uint32_t sg = stage_of(i);
+                const int32_t kx = (int32_t)(sg * 128);
                 tc::tma_load_2d(st, &map_w, kx, (int32_t)row0, &full_t[slot]);
                 tc::tma_load_2d(st + G.b_off, &map_a, kx, (int32_t)tok0, &full_t[slot]);
+                if (pre) {
+                    bulk_g2s(st + G.sfa_off, a.sw_img + ((size_t)blockIdx.y * kst + sg) * sw_bytes, sw_bytes, &full_t[slot]);
+                    bulk_g2s(st + G.sfb_off, a.sa_img + ((size_t)blockIdx.x * kst + sg) * sa_bytes, sa_bytes, &full_t[slot]);
+                }
                 issued = i + 1;
             }
             // Never leave with copies in flight: wait for the last use of each slot.
@@ -278,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = NV ? tc::idesc_nvf4(a.nt) : tc::idesc_mxf4(a.nt);
             for (uint32_t i = 0; i < nst; ++i) {
                 const uint32_t slot = i % S, par = (i / S) & 1;
-                if (!wait_or_abort(&full_t[slot], par, abort) || !wait_or_abort(&full_s[slot], par, abort)) break;
+                if (!wait_or_abort(&full_t[slot], par, abort) || (!pre && !wait_or_abort(&full_s[slot], par, abort)))
+                    break;
                 tc::fence_after_sync();
                 const uint8_t *st = smem + slot * G.stage_bytes;
                 const uint32_t sa_col = tbase + G.sfa_col0 + slot * 4 * G.ak;
@@ -326,8 +363,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (G.sfb_atoms > 1 && t + 128 < a.nt) b1 = load(a.sa, tok0 + t + 128, a.m, kb0);
         };
 #pragma unroll
-        for (uint32_t j = 0; j < kScaleAhead; ++j) fetch(j, rw[j], rb0[j], rb1[j]);
-        for (uint32_t i = 0; i < nst; ++i) {
+        for (uint32_t j = 0; j < kScaleAhead; ++j)
+            if (!pre) fetch(j, rw[j], rb0[j], rb1[j]);
+        for (uint32_t i = 0; i < (pre ? 0u : nst); ++i) {
             const uint32_t slot = i % S;
             if (i >= S && !wait_or_abort(&empty[slot], ((i / S) - 1) & 1, abort)) break;
             uint8_t *st = smem + slot * G.stage_bytes;
@@ -473,7 +511,7 @@ inline size_t partials_bytes(const Plan &p, uint32_t m, uint32_t n, uint32_t ter
 // partials: split-K scratch of partials_bytes() (unused when p.splits == 1).
 int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a, const uint8_t *sa,
            const uint8_t *w, const uint8_t *sw, void *d, Mode mode, const Plan &p, uint32_t terms, float *partials,
-           bool nv = false, float alpha = 1.0f) {
+           bool nv = false, float alpha = 1.0f, const uint8_t *sa_img = nullptr, const uint8_t *sw_img = nullptr) {
     CUtensorMap map_w, map_a;
     if (!tc::make_map_sw128(&map_w, w, k / 2, n, 128) || !tc::make_map_sw128(&map_a, a, k / 2, m, p.nt)) {
         set_error("fp4_mma: cuTensorMapEncodeTiled failed (m=%u n=%u k=%u)", m, n, k);
@@ -496,7 +534,7 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
         set_error("fp4_mma: split-K launch without a workspace");
         return FP4X_EINVAL;
     }
-    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials, alpha};
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials, alpha, sa_img, sw_img};
     const dim3 grid(p.m_tiles, p.n_tiles, p.splits);
     if (nv)
         mxf4_gemm_kernel<true><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, args);
