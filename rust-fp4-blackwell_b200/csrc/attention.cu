@@ -432,26 +432,83 @@ cudaError_t launch_mma(cudaStream_t stream, const Params &p, dim3 grid, bool pdl
     return cudaLaunchKernelEx(&cfg, attn_mma_kernel<HD, HPC, QT, OT>, p);
 }
 
-// grid = (n_heads, batch), block = HD: merge the slices of one (b, head).
+constexpr int kCombineThreads = 256, kCombineDims = 16;
+
+// Block-wide max / sum of one value per thread, in a fixed order (the result does
+// not depend on timing). `red` holds one float per warp.
+__device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
+    for (int o = 16; o; o >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = is_max ? fmaxf(v, w) : v + w;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = red[0];
+    for (int w = 1; w < kCombineThreads / 32; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
+    return v;
+}
+
+// grid = (n_heads, batch, HD / kCombineDims), block = kCombineThreads: merge the
+// slices of one (b, head) for kCombineDims of its output dims.  The block finds the
+// slices' common max M, then walks the slices in chunks of kCombineThreads: each
+// thread loads its kCombineDims slices' outputs (one dim each) first, turns one
+// slice's max into its weight exp(m_s - M) (shared memory), and adds its weighted
+// outputs; the per-thread sums of a dim are added in a fixed order at the end.
+// Every load of a chunk is issued before the first one is used, so a few hundred
+// slices cost about two L2 round trips, not one per slice.
 template <int HD, typename OT>
-__global__ void attn_combine_kernel(Params p) {
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(Params p) {
+    constexpr int T = kCombineThreads, DB = kCombineDims, G = T / DB;
+    static_assert(HD % DB == 0 && T % DB == 0, "combine tiling");
+    __shared__ float wgt[T];
+    __shared__ float red[T / 32];
+    __shared__ float part[G][DB];
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const uint32_t h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const uint32_t g = tid / DB, d = blockIdx.z * DB + tid % DB;
     const size_t bh = (size_t)b * p.n_heads + h;
     const float *rec = p.ws + bh * p.splits * (HD + 2);
     const uint32_t seq = seq_of(p, b);
     const uint32_t used = (seq + p.split_len - 1) / p.split_len;
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < used; ++s) M = fmaxf(M, rec[s * (HD + 2)]);
-    float L = 0.0f, O = 0.0f;
-    for (uint32_t s = 0; s < used; ++s) {
-        const float *r = rec + s * (HD + 2);
-        const float f = __expf(r[0] - M);
-        L += r[1] * f;
-        O += r[2 + d] * f;
+    float m = -INFINITY;
+    for (uint32_t s = tid; s < used; s += T) m = fmaxf(m, rec[(size_t)s * (HD + 2)]);
+    const float M = block_reduce(m, red, true);
+    float l = 0.0f, o = 0.0f;
+    for (uint32_t base = 0; base < used; base += T) {
+        const uint32_t cnt = min((uint32_t)T, used - base);
+        const float *r = rec + (size_t)base * (HD + 2) + 2 + d;
+        float v[T / G];
+#pragma unroll
+        for (int k = 0; k < T / G; ++k) {
+            const uint32_t j = g + k * G;
+            v[k] = j < cnt ? r[(size_t)j * (HD + 2)] : 0.0f;
+        }
+        float f = 0.0f;
+        if (tid < cnt) {
+            const float *rs = rec + (size_t)(base + tid) * (HD + 2);
+            f = __expf(rs[0] - M);
+            l += rs[1] * f;
+        }
+        __syncthreads();  // the previous chunk's weights are no longer read
+        wgt[tid] = f;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < T / G; ++k) {
+            const uint32_t j = g + k * G;
+            if (j < cnt) o += v[k] * wgt[j];
+        }
     }
-    store_out(reinterpret_cast<OT *>(p.out) + bh * HD + d, O / L);
+    const float L = block_reduce(l, red, false);
+    part[g][tid % DB] = o;
+    __syncthreads();
+    if (tid < DB) {
+        float O = part[0][tid];
+#pragma unroll
+        for (int k = 1; k < G; ++k) O += part[k][tid];
+        store_out(reinterpret_cast<OT *>(p.out) + bh * HD + d, O / L);
+    }
 }
 
 // q heads per CTA: the whole GQA group when it is 4 or 8 (else 8 or 4 of it, else 1).
@@ -466,13 +523,38 @@ size_t workspace_bytes(uint32_t batch, uint32_t n_heads, uint32_t head_dim, uint
     return splits <= 1 ? 0 : (size_t)batch * n_heads * splits * (head_dim + 2) * sizeof(float);
 }
 
-// Slices so that batch * head-groups * slices covers the SMs ~4x, each slice >= 128 tokens.
-uint32_t choose_splits(uint32_t batch, uint32_t groups, uint32_t seq) {
-    const uint32_t ctas = batch * groups;
-    const uint32_t target = (uint32_t)num_sms() * 4;
-    uint32_t s = std::max<uint32_t>(1, (target + ctas - 1) / ctas);
-    s = std::min<uint32_t>(s, std::max<uint32_t>(1, seq / 128));
-    return std::min<uint32_t>(s, 256);
+// Slices per (row, head group), from a wave model of the split kernel: a CTA walks
+// its slice one 64-token tile at a time, and a tile costs the larger of the CTA's
+// own time per tile (0.9 us at head_dim 64, 1.17 us at 128: issue and latency
+// bound) and the HBM time of one tile of every CTA resident in that wave (at
+// 6.5 TB/s); each CTA adds a prologue/epilogue cost (1.5 / 3 us), CTAs past the
+// resident slots (CTAs per SM, from the kernel's shared memory, x SMs) run in
+// further waves, and more than one slice adds the combine launch.  The
+// constants were fitted to split-count sweeps on B200 (batch 1 and 8, contexts
+// 2k-32k); the model keeps the last wave from holding a handful of CTAs.
+uint32_t choose_splits(uint32_t batch, uint32_t groups, uint32_t seq, uint32_t hd) {
+    if (seq <= 64) return 1;
+    const bool wide = hd > 64;
+    const double smem = wide ? (double)MmaCfg<128>::kSmem : (double)MmaCfg<64>::kSmem;
+    const double slots = std::max(1.0, std::floor(233472.0 / (smem + 1024.0))) * num_sms();
+    const double tile_bytes = 64.0 * hd * 2 * 2, tile_own = wide ? 1.17 : 0.9, cta_fixed = wide ? 3.0 : 1.5;
+    double best = 0.0;
+    uint32_t pick = 1;
+    for (uint32_t s = 1; s <= 256; ++s) {
+        const uint32_t len = (seq + s - 1) / s;
+        if (s > 1 && len < 64) break;
+        const uint32_t used = (seq + len - 1) / len;
+        if (used != s) continue;  // same geometry as a smaller count
+        const double tiles = (double)((len + 63) / 64);
+        double left = (double)batch * groups * s, t = s > 1 ? 1.0 + 0.01 * s : 0.0;
+        while (left > 0) {
+            const double n = std::min(left, slots);
+            t += tiles * std::max(tile_own, n * tile_bytes / 6.5e6) + cta_fixed;
+            left -= n;
+        }
+        if (s == 1 || t < best - 1e-9) best = t, pick = s;
+    }
+    return pick;
 }
 
 template <typename QT, typename KT, typename OT>
@@ -487,7 +569,7 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
     const uint32_t hpc = heads_per_cta(group, group_heads);
     uint32_t splits = 1;
     if (ws) {
-        splits = choose_splits(batch, n_heads / hpc, seq);
+        splits = choose_splits(batch, n_heads / hpc, seq, hd);
         while (splits > 1 && workspace_bytes(batch, n_heads, hd, splits) > ws_bytes) splits /= 2;
     }
     Params p;
@@ -509,15 +591,15 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
             return FP4X_ECUDA;
         }
         if (p.splits > 1) {
-            if (hd == 64) attn_combine_kernel<64, OT><<<dim3(n_heads, batch), 64, 0, stream>>>(p);
-            else attn_combine_kernel<128, OT><<<dim3(n_heads, batch), 128, 0, stream>>>(p);
+            if (hd == 64) attn_combine_kernel<64, OT><<<dim3(n_heads, batch, 64 / kCombineDims), kCombineThreads, 0, stream>>>(p);
+            else attn_combine_kernel<128, OT><<<dim3(n_heads, batch, 128 / kCombineDims), kCombineThreads, 0, stream>>>(p);
         }
         return check_launch("llama_attn_decode");
     }
 #define FP4X_ATTN_CASE(HD_, HPC_)                                                                       \
     if (hd == HD_ && hpc == HPC_) {                                                                   \
         attn_split_kernel<HD_, HPC_, QT, KT, OT><<<grid, kThreads, 0, stream>>>(p);                   \
-        if (p.splits > 1) attn_combine_kernel<HD_, OT><<<dim3(n_heads, batch), HD_, 0, stream>>>(p); \
+        if (p.splits > 1) attn_combine_kernel<HD_, OT><<<dim3(n_heads, batch, HD_ / kCombineDims), kCombineThreads, 0, stream>>>(p); \
     }
     FP4X_ATTN_CASE(64, 1)
     FP4X_ATTN_CASE(64, 4)
@@ -547,8 +629,8 @@ int launch_engine_t(cudaStream_t stream, const Params &p, bool pdl) {
                                             : cudaLaunchKernelEx(&cfg, attn_split_kernel<HD, HPC, float, uint16_t, float>, p);
     if (e == cudaSuccess && p.splits > 1) {
         cudaLaunchConfig_t c2 = cfg;
-        c2.gridDim = dim3(p.n_heads, p.batch);
-        c2.blockDim = dim3(HD);
+        c2.gridDim = dim3(p.n_heads, p.batch, HD / kCombineDims);
+        c2.blockDim = dim3(kCombineThreads);
         e = cudaLaunchKernelEx(&c2, attn_combine_kernel<HD, float>, p);
     }
     if (e != cudaSuccess) {
@@ -594,7 +676,7 @@ extern "C" size_t llama_attn_workspace_size(uint32_t batch, uint32_t n_heads, ui
                                             uint32_t seq) {
     if (n_kv_heads == 0 || n_heads % n_kv_heads) return 0;
     const uint32_t hpc = attn::heads_per_cta(n_heads / n_kv_heads, true);
-    return attn::workspace_bytes(batch, n_heads, head_dim, attn::choose_splits(batch, n_heads / hpc, seq));
+    return attn::workspace_bytes(batch, n_heads, head_dim, attn::choose_splits(batch, n_heads / hpc, seq, head_dim));
 }
 
 extern "C" int llama_attn_decode_bf16(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,

@@ -355,36 +355,6 @@ __device__ __forceinline__ int term_words8(float (&x)[8], uint32_t (&words)[8]) 
     return e1;
 }
 
-__device__ __forceinline__ void decompose_word8(float (&x)[8], uint32_t b, uint32_t w, bool valid, uint8_t *B,
-                                                uint8_t *sfb, bool pairs) {
-    uint32_t words[8];
-    const int e1 = term_words8(x, words);
-    if (!valid) return;
-    // term order rotated by block: the 8 blocks of a warp (128 bytes apart) then hit
-    // 8 different bank groups instead of one
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-        const uint32_t t = (r + b) & 7u;
-        uint32_t wv = words[0];
-#pragma unroll
-        for (int q = 1; q < 8; ++q) wv = t == (uint32_t)q ? words[q] : wv;
-        *reinterpret_cast<uint32_t *>(B + b * 128 + t * 16 + w * 4) = wv;
-    }
-    if (w == 0) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint8_t sb = (uint8_t)(term_exp(e1, t) + 127);
-            if (!pairs) {
-                sfb[(b >> 2) * 128 + t * 16 + (b & 3)] = sb;
-            } else {
-                uint8_t *q2 = sfb + (b >> 1) * 128 + t * 16 + 2 * (b & 1);
-                q2[0] = sb;
-                q2[1] = sb;
-            }
-        }
-    }
-}
-
 // The same 8-term decomposition with one value per lane (warp w: 32-blocks w,
 // w + kCW, ...; same arithmetic per value as term_words8, so the same bits), for
 // short vectors: the serial term chain per thread is 8x shorter and 8x more
@@ -429,25 +399,6 @@ __device__ void decompose_lanes(const float *v, uint32_t K, uint8_t *B, uint8_t 
                 q2[1] = sb;
             }
         }
-    }
-}
-
-// Decomposition of v[0, K) in shared memory (K % 32 == 0), one word per thread.
-__device__ void decompose8(const float *v, uint32_t K, uint8_t *B, uint8_t *sfb, bool pairs) {
-    const uint32_t nw = K / 8, lane = threadIdx.x & 31;
-    for (uint32_t base = threadIdx.x - lane; base < nw; base += kCons) {
-        const uint32_t i = base + lane;
-        const bool valid = i < nw;  // the 4 words of a block are valid together
-        float x[8];
-        if (valid) {
-            const float4 p0 = *reinterpret_cast<const float4 *>(v + 8 * i);
-            const float4 p1 = *reinterpret_cast<const float4 *>(v + 8 * i + 4);
-            x[0] = p0.x, x[1] = p0.y, x[2] = p0.z, x[3] = p0.w, x[4] = p1.x, x[5] = p1.y, x[6] = p1.z, x[7] = p1.w;
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) x[j] = 0.0f;
-        }
-        decompose_word8(x, i >> 2, i & 3, valid, B, sfb, pairs);
     }
 }
 
