@@ -707,14 +707,18 @@ __device__ void fold_delta(Ctx &c, uint32_t l) {
     }
 }
 
-// O projection of the attention output staged in xv ([head slot][hd] f32).
-__device__ void o_projection(Ctx &c, uint32_t lay_count) {
+// O projection of the attention output staged in xv ([head slot][hd] f32).  With
+// fold_l >= 0 the previous layer's FFN delta is folded into X (fold_delta) while
+// the O MMAs run: nothing in phase B reads X before the O epilogue, and both add
+// into X.
+__device__ void o_projection(Ctx &c, uint32_t lay_count, int fold_l = -1) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
     decompose_lanes(reinterpret_cast<const float *>(c.smem + c.L.xv), S.nh * p.hd, c.smem + c.L.bo,
                     c.smem + c.L.sfbo, false);
     signal_operand(c, PH_O);
     CST(8);
+    if (fold_l >= 0) fold_delta(c, (uint32_t)fold_l);
     wait_acc(c, PH_O, lay_count & 1);
     CST(9);
     if (!c.ok) return;
@@ -731,8 +735,10 @@ __device__ void o_projection(Ctx &c, uint32_t lay_count) {
 __device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
-    fold_delta(c, l);
-    if (S.n_pairs == 0) return;
+    if (S.n_pairs == 0) {
+        fold_delta(c, l);
+        return;
+    }
     if (p.hd == 64) {
         stage_qkv<64>(c, l, pos);
         CST(6);
@@ -743,7 +749,7 @@ __device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_coun
         attend<128>(c, l, pos);
     }
     CST(7);
-    o_projection(c, lay_count);
+    o_projection(c, lay_count, (int)l);
 }
 
 // Split attention for long contexts, part 1: unit u = (KV head g, slice s) of the
