@@ -1527,11 +1527,20 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
             i0 += b1 - b0;
         }
     }
-    // O: (head, 128-row tile) pairs, head-major, split evenly over the light CTAs
-    const uint32_t npairs = c.n_heads * otile;
+    // O: (head, 128-row tile) pairs, head-major, over the light CTAs.  When every
+    // head can have the same number of CTAs (cph), each CTA takes pairs of one head
+    // only, so every CTA with O work attends exactly one head (phase B balanced);
+    // otherwise the pairs are split evenly.
+    const uint32_t npairs = c.n_heads * otile, cph = NL / c.n_heads;
+    const bool by_head = cph >= 1 && (otile + cph - 1) / cph <= (uint32_t)kMaxPairs;
     for (uint32_t k = 0; k < NL; ++k) {
         Sched &s = S[light[k]];
-        const uint32_t p0 = (uint32_t)((uint64_t)npairs * k / NL), p1 = (uint32_t)((uint64_t)npairs * (k + 1) / NL);
+        uint32_t p0 = (uint32_t)((uint64_t)npairs * k / NL), p1 = (uint32_t)((uint64_t)npairs * (k + 1) / NL);
+        if (by_head) {
+            const uint32_t h = k / cph, j = k % cph;
+            p0 = p1 = 0;
+            if (h < c.n_heads) p0 = h * otile + otile * j / cph, p1 = h * otile + otile * (j + 1) / cph;
+        }
         if (p1 - p0 > (uint32_t)kMaxPairs) PTC_UNSUPPORTED("tensor-core decode: too many O pairs per CTA");
         for (uint32_t q = p0; q < p1; ++q) {
             s.pair_head[s.n_pairs] = q / otile;
