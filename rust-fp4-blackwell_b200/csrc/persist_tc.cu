@@ -1117,8 +1117,12 @@ __device__ bool run_ops(const Params &p, const Sched &S, const ChunkOp *ops, uin
             tstamp(tsb + 19 + (cur == PH_LM ? 0 : cur));
             tc::fence_after_sync();
             bo = operand_of(cur, p, S, smem, L);
-            for (uint32_t a = 0; a < bo.atoms; ++a)
-                tc::utccp_scale_atom(tbase + p.sfb_col0 + 4 * a, tc::smem_desc(bo.sfb + 128 * a, 128, 128, 0));
+            // only the atoms this CTA's blocks read (a QKV unit's k-range needs a few)
+            for (uint32_t r = 0; r < 4; r += 2) {
+                const uint32_t a0 = S.batoms[cur][r], a1 = a0 + S.batoms[cur][r + 1];
+                for (uint32_t a = a0; a < a1; ++a)
+                    tc::utccp_scale_atom(tbase + p.sfb_col0 + 4 * a, tc::smem_desc(bo.sfb + 128 * a, 128, 128, 0));
+            }
         }
         const uint32_t slot = seq % kMaxSlots;
         uint64_t vstart;
@@ -1659,6 +1663,30 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
         s.lm_bytes = off - m0;
         if (s.n_ops > (uint32_t)kMaxOps || s.n_lm_ops > (uint32_t)kMaxLmOps)
             PTC_UNSUPPORTED("tensor-core decode: too many chunks per CTA");
+        // B scale atoms per phase (atom a covers k blocks 2a, 2a + 1 of the operand) as
+        // at most two runs; more than two runs are copied as their hull
+        uint64_t used[PH_N] = {};
+        for (int lmp = 0; lmp < 2; ++lmp) {
+            const ChunkOp *ops = lmp ? s.lm_ops : s.ops;
+            const uint32_t n = lmp ? s.n_lm_ops : s.n_ops;
+            for (uint32_t i = 0; i < n; ++i) {
+                const ChunkOp &op = ops[i];
+                const uint32_t klast = op.bk0 + std::min<uint32_t>(op.nblk, op.bpa) - 1;
+                if ((klast >> 1) >= 64) PTC_UNSUPPORTED("tensor-core decode: operand wider than 64 scale atoms");
+                for (uint32_t a = op.bk0 >> 1; a <= (klast >> 1); ++a) used[op.phase] |= 1ull << a;
+            }
+        }
+        for (int ph = 0; ph < PH_N; ++ph) {
+            std::vector<std::pair<uint32_t, uint32_t>> runs;  // (start, count)
+            for (uint32_t a = 0; a < 64; ++a)
+                if ((used[ph] >> a) & 1u) {
+                    if (!runs.empty() && runs.back().first + runs.back().second == a) ++runs.back().second;
+                    else runs.push_back({a, 1});
+                }
+            if (runs.size() > 2) runs = {{runs.front().first, runs.back().first + runs.back().second - runs.front().first}};
+            for (size_t r = 0; r < runs.size(); ++r)
+                s.batoms[ph][2 * r] = (uint8_t)runs[r].first, s.batoms[ph][2 * r + 1] = (uint8_t)runs[r].second;
+        }
     }
     // shared and tensor memory
     Params P = {};

@@ -69,6 +69,10 @@ struct Sched {
     uint64_t layer_bytes, lm_bytes;
     ChunkOp ops[kMaxOps];
     ChunkOp lm_ops[kMaxLmOps];
+    // per phase: the B scale atoms this CTA's blocks read, as up to two runs
+    // (start, count, start, count), copied at phase start
+    uint8_t batoms[PH_N][4];
+    uint8_t pad2[4];
 };
 
 struct Params {
