@@ -166,35 +166,6 @@ def test_engine_tinyllama_config1(path):
     print(f"config1: worst logits rel err {worst:.3e}")
 
 
-def test_engine_llama8b_shape_paths_agree():
-    """BASELINE config 4 shape at TP = 1 (32 layers, d 4096, ffn 14336, 32q/8kv hd 128,
-    vocab 128256): the tensor-core persistent path against the CUDA-graph path (whose
-    kernels are checked against the oracle on the smaller shapes) on the same device
-    state.  Two results each within 1e-2 of the oracle differ by up to 2e-2 (the bf16
-    KV cache rounds the two paths' K/V sums, equal to ~1e-7, to possibly different
-    bf16 neighbours, and 32 layers compound it), so the bound here is 2e-2."""
-    cfg = dict(engine.LLAMA3_8B, max_seq=64)
-    toks = oracle.uniform_ids(11, cfg["vocab"], 6)
-    with engine.Model(cfg) as m:
-        assert m.path == "tensor", m.path
-        outs = {}
-        for path in ("graph", "tensor"):
-            m.set_path(path)
-            m.reset()
-            outs[path] = [m.forward(int(t), pos) for pos, t in enumerate(toks)]
-        for (ng, lg), (nt, lt) in zip(outs["graph"], outs["tensor"]):
-            compare_logits(lt, lg, tol=2 * LOGIT_TOL)
-        ids_g, ids_t = None, None
-        prompt = oracle.uniform_ids(12, cfg["vocab"], 4)
-        m.set_path("graph")
-        m.reset()
-        ids_g, _, _ = m.generate(prompt, 8)
-        m.set_path("tensor")
-        m.reset()
-        ids_t, _, _ = m.generate(prompt, 8)
-        assert np.mean(ids_t == ids_g) >= 0.75, (ids_t, ids_g)  # near-ties may flip a token
-
-
 @pytest.mark.parametrize("cfg", [TINY, TINY128], ids=["hd64", "hd128"])
 def test_engine_long_context_split_attention(cfg):
     """Contexts above 512 positions switch the tensor path's attention to (KV head,
