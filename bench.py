@@ -146,6 +146,7 @@ DTYPES = {
 def cpu_baseline_port(cfg, budget_s=20.0, threads=0):
     """Oracle forward (reference CPU loops, OpenMP over rows) on a bounded sample."""
     import oracle
+    threads = threads if threads > 0 else host_cores()
     m = oracle.Model(cfg, threads=threads)
     from fp4x import synth
     prompt = synth.prompt_for(cfg)
@@ -160,19 +161,32 @@ def cpu_baseline_port(cfg, budget_s=20.0, threads=0):
         tok = int(prompt[pos + 1]) if pos + 1 < len(prompt) else nxt
     dt = time.perf_counter() - t0
     m.close()
-    cores = threads if threads > 0 else oracle.max_threads()
-    return {"value": n / dt, "unit": UNIT, "cores": cores, "kind": "port",
+    return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{n} single-token forwards (positions 1..{n}) of the TinyLlama-shape MXFP4 model, "
                       f"C oracle of the reference loops, OpenMP over rows"}
 
 
+def host_cores() -> int:
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1 for its
+    workers, so the OpenMP default is not the box's core count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def run_reference(args):
+    """The reference's CPU path on the whole host: one process over every host core
+    (rank 0; under torchrun the other ranks exit without work).  N GPU replicas on
+    this box would share the same cores, so the line is the host's CPU throughput
+    at every N."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import oracle
     cfg = tinyllama_cfg()
-    m = oracle.Model(cfg)
+    cores = host_cores()
+    m = oracle.Model(cfg, threads=cores)
     from fp4x import synth
     prompt = synth.prompt_for(cfg)
     # prefill (untimed) then W warm-up and K timed decode tokens, as our arm
@@ -191,7 +205,6 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     m.close()
     v = args.steps / dt
-    cores = oracle.max_threads()
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
@@ -201,7 +214,8 @@ def run_reference(args):
                    "batch": 1, "prompt": N_PROMPT, "positions": f"{N_PROMPT}..{N_PROMPT + args.warmup + args.steps - 1}"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": "the whole --steps run: single-token forwards of the C restatement of the "
-                                   "reference CPU loops (Rust/cuda-oxide reference not buildable here)"},
+                                   "reference CPU loops (Rust/cuda-oxide reference not buildable here), one "
+                                   f"process over all {cores} host cores (OpenMP over rows), rank 0 only"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -502,6 +516,114 @@ def run_batch(args):
     return 0
 
 
+def tp_section(args, rank, world, torch, dist):
+    """BASELINE config 4 over the job's ranks (tensor parallel at TP = world; one
+    process per GPU, the library's NVLink peer-memory allreduce after O and down):
+      parity  a 2-layer model of the 8B shape (every real dimension): each rank's
+              logits slice over 3 positions, gathered on rank 0 and compared with
+              the CPU oracle's full logits (rms-floor relative error, greedy token);
+      bs1     batch-1 greedy decode at a 4096-token context (zero-filled KV);
+      bs64    64 sequences at a 4096-token context through the batched engine.
+    Times are CUDA events on the launching stream, max over ranks.  Every rank takes
+    the same steps in the same order; rank 0 returns the summary."""
+    from fp4x import engine, tp
+    import numpy as np
+    group = dist.new_group(backend="gloo") if dist else None
+    st = torch.cuda.current_stream()
+    out = {"tp": world, "model": "llama3-8b shape, MXFP4, random init", "context": args.tp_ctx}
+
+    def barrier():
+        if dist:
+            dist.barrier(group=group)
+
+    def make(cfg):
+        return tp.create_model(cfg, group=group) if dist else engine.Model(cfg)
+
+    def max_over_ranks(t):
+        if dist:
+            tt = torch.tensor([t], dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
+            t = float(tt.item())
+        return t
+
+    # parity at reduced depth
+    pcfg = dict(engine.LLAMA3_8B, n_layers=2, max_seq=16)
+    toks = [int(t) for t in np.random.default_rng(4).integers(0, pcfg["vocab"], 3)]
+    m = make(pcfg)
+    v0, _ = m.shard()
+    mine = []
+    for pos, t in enumerate(toks):
+        nxt, lg = m.forward(t, pos)
+        mine.append((nxt, v0, lg))
+    m.close()
+    parts = [None] * world
+    if dist:
+        dist.all_gather_object(parts, mine, group=group)
+    else:
+        parts = [mine]
+    if rank == 0:
+        import oracle
+        ref = oracle.Model(pcfg, threads=host_cores())
+        worst, same = 0.0, True
+        for pos, t in enumerate(toks):
+            rn, rl = ref.forward(t, pos)
+            full = np.empty_like(rl)
+            for pr in parts:
+                _, a, lg = pr[pos]
+                full[a:a + len(lg)] = lg
+            rms = float(np.sqrt(np.mean(rl.astype(np.float64) ** 2)))
+            worst = max(worst, float(np.max(np.abs(full.astype(np.float64) - rl) / np.maximum(np.abs(rl), rms))))
+            same = same and all(pr[pos][0] == rn for pr in parts)
+        ref.close()
+        out["parity"] = {"layers": 2, "positions": len(toks), "max_rel_logits": worst, "tol": 1e-2,
+                         "greedy_tokens_equal": bool(same), "vs": "CPU oracle (reference loops restated)"}
+    barrier()
+
+    # batch 1 at the full depth
+    ctx = args.tp_ctx
+    cfg = dict(engine.LLAMA3_8B, max_seq=ctx + args.warmup + max(args.tp_steps, args.tp_bsteps) + 8)
+    m = make(cfg)
+    out["path_bs1"] = m.path
+    m.forward(1, ctx - 1, want_logits=False)
+    m.decode_steps(args.warmup)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    m.decode_steps(args.tp_steps)
+    e1.record(st)
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
+    out["bs1_tok_s"] = args.tp_steps / t
+    out["bs1_ms_per_token"] = 1e3 * t / args.tp_steps
+    out["bs1_steps"] = args.tp_steps
+    out["weight_bytes_per_rank"] = m.weight_bytes()
+
+    # batch 64
+    B = args.tp_batch
+    b = tp.create_batch(m, B, group=group) if dist else engine.Batch(m, B)
+    for s in range(B):
+        b.set_length(s, ctx, (17 + 31 * s) % cfg["vocab"])
+    b.decode(args.warmup)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(st)
+    b.decode(args.tp_bsteps)
+    e1.record(st)
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3)
+    out[f"bs{B}_tok_s"] = B * args.tp_bsteps / t
+    out[f"bs{B}_ms_per_step"] = 1e3 * t / args.tp_bsteps
+    out[f"bs{B}_steps"] = args.tp_bsteps
+    b.close()
+    m.close()
+    torch.cuda.synchronize()
+    barrier()
+    if dist:
+        dist.destroy_process_group(group)
+    return out if rank == 0 else None
+
+
 def gemv_config0(torch, peak):
     """Config 0 GEMV (fp4_gemv through the C ABI) over 64 rotated weight copies,
     captured in one CUDA graph (no host launch gaps), CUDA-event timed."""
@@ -532,13 +654,42 @@ def gemv_config0(torch, peak):
     e1.record(st)
     torch.cuda.synchronize()
     per = e0.elapsed_time(e1) / (reps * copies) * 1e-3
+    # one launch at a time (each bracketed by its own events, weights not in L2 since
+    # the 63 other copies ran in between): the kernel without the graph's launch chain
+    singles = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ws]
+    with torch.cuda.stream(s):
+        for (a, b), (p, sc) in zip(ev, ws):
+            a.record(s)
+            ops.gemv(p, sc, x, out=y)
+            b.record(s)
+    torch.cuda.synchronize()
+    singles = sorted(a.elapsed_time(b) * 1e3 for a, b in ev)
     nbytes = n * k // 2 + n * k // 32 + k * 2 + n * 4
     gbs = nbytes / per / 1e9
     del g, ws
     return {"workload": "config0: MXFP4 GEMV 5632x2048, bf16 x, f32 y, 64 rotated weight copies (394 MB > L2) "
                         "in one CUDA graph",
             "bytes_per_launch": nbytes, "us_per_launch": per * 1e6, "achieved_gbs": gbs, "peak_gbs": peak,
-            "frac": gbs / peak}
+            "frac": gbs / peak, "us_single_launch_median": singles[len(singles) // 2],
+            "single_launch_note": "each of the 64 copies launched alone between two events on one stream"}
+
+
+def run_config0(args):
+    """BASELINE config 0 alone: fp4_gemv 5632x2048 over 64 rotated weight copies in
+    one CUDA graph (the `gemv` key of the default line), printed as its own line."""
+    import torch
+    peak, peak_kind = hbm_peak()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        g = gemv_config0(torch, peak)
+    line = {"metric": "config0 fp4_gemv 5632x2048 HBM GB/s", "value": g["achieved_gbs"], "unit": "GB/s",
+            "higher_is_better": True, "us_per_launch": g["us_per_launch"],
+            "roofline": {"bound": "hbm", "achieved": g["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": g["frac"], "bytes_per_launch": g["bytes_per_launch"], "peak_kind": peak_kind},
+            "dtype": "e2m1xe8m0 weights, bf16 x, f32 accumulate", "data": "synthetic (seeded N(0,0.02) -> MXFP4)",
+            "config": {"workload": g["workload"]}, "detail": g, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -553,6 +704,7 @@ def main():
     ap.add_argument("--c3-m", default="16,64,256,512")
     ap.add_argument("--config2", action="store_true", help="attention sweep of BASELINE config 2 instead of decode")
     ap.add_argument("--config4", action="store_true", help="Llama-3-8B-shape TP decode (torchrun ranks) instead")
+    ap.add_argument("--config0", action="store_true", help="the config-0 fp4_gemv measurement alone")
     ap.add_argument("--c4-ctx", type=int, default=4096)
     ap.add_argument("--c2-ctx", default="512,2048,8192,32768")
     ap.add_argument("--c2-batch", default="1,8,64")
@@ -562,6 +714,11 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="batched decode of this many sequences instead")
     ap.add_argument("--batch-model", default="llama8b", choices=["llama8b", "tinyllama"])
     ap.add_argument("--batch-ctx", type=int, default=4096)
+    ap.add_argument("--no-tp", action="store_true", help="skip the config-4 tensor-parallel section")
+    ap.add_argument("--tp-ctx", type=int, default=4096)
+    ap.add_argument("--tp-steps", type=int, default=32, help="timed batch-1 tokens of the TP section")
+    ap.add_argument("--tp-bsteps", type=int, default=8, help="timed batch steps of the TP section")
+    ap.add_argument("--tp-batch", type=int, default=64)
     ap.add_argument("--profile-region", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = ap.parse_args()
@@ -574,6 +731,8 @@ def main():
         return run_config2(args)
     if args.config4:
         return run_config4(args)
+    if args.config0:
+        return run_config0(args)
     if args.batch:
         return run_batch(args)
 
@@ -651,6 +810,11 @@ def main():
     if rank == 0:
         gemv = gemv_config0(torch, peak)
     model.close()
+    torch.cuda.synchronize()
+
+    tpres = None
+    if not args.no_tp:
+        tpres = tp_section(args, rank, world, torch, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -672,6 +836,7 @@ def main():
                      "traffic": TRAFFIC_PER_TOKEN.get(model_path), "bytes_per_launch": wbytes,
                      "peak_kind": peak_kind, "traffic_source": "ncu dram bytes of a 20-token launch / 20"},
         "gemv": gemv,
+        "tp": tpres,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": kpt * args.steps if model_path == "graph" else 1,
