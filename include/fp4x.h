@@ -53,6 +53,16 @@ FP4X_API const char *fp4x_version(void);
 /* Synchronises `stream`, then reads and clears the device error word that
  * kernels set when a bounded wait expires.  Returns FP4X_ETIMEOUT if set. */
 FP4X_API int fp4x_device_error(fp4x_stream_t stream, uint32_t *bits_out);
+/* Poll bound of the device-side waits on flags that another rank raises (the
+ * tensor-parallel exchanges and cross-rank grid barriers) on the CURRENT device;
+ * 0 restores each wait's compiled default (about 2 s).  A wait that runs out sets
+ * the device error word and the kernel returns, so fp4x_device_error() reports
+ * FP4X_ETIMEOUT and the context stays usable.  Replaces the reference's unwrap()
+ * panic on a failed launch or sync (examples/llama_run/src/main.rs:513-535) for
+ * the multi-GPU case the reference does not have: a rank that stopped issuing is
+ * detected in about `polls` x 0.1 us instead of hanging the others.  Not
+ * synchronised with kernels already in flight. */
+FP4X_API int fp4x_set_wait_limit(uint32_t polls);
 
 /* ------------------------------------------------------------ formats */
 
@@ -106,8 +116,9 @@ FP4X_API int fp4_gemv_f32x(fp4x_stream_t stream, uint32_t n, uint32_t k, const u
  * fp4_mma_allones (examples/fp4_mma/src/main.rs:18-54, sm_120a mma.sync); this
  * is the batched-decode / prefill GEMM built on it.  k must be a multiple of 64;
  * a and w 16-byte aligned.  When the tile grid is too small to fill the GPU the
- * K range is split: each split writes fp32 partial sums to the workspace and the
- * last CTA of a tile to finish adds them in split order (deterministic), so the
+ * K range is split: each split stores its fp32 partial tile in the workspace
+ * (plain stores, no atomics) and a second kernel (splitk_reduce_kernel, same
+ * stream) adds the splits in split order and writes d (deterministic), so the
  * workspace holds fp4_mma_workspace_size(m, n, k) bytes (0 = none needed; may
  * then be NULL). */
 FP4X_API size_t fp4_mma_workspace_size(uint32_t m, uint32_t n, uint32_t k);
@@ -196,9 +207,11 @@ FP4X_API int llama_attn_decode_bf16(fp4x_stream_t stream, uint32_t batch, uint32
  * cudaFree).  The split-KV partials live in one static device array of
  * llama_attn_noalloc_max_bytes() bytes (4 MiB) that every GPU loading the
  * library keeps until exit; a shape needing more returns FP4X_EINVAL.  The
- * first call on each device looks the array up (make it before any stream
- * capture).  Calls share the array: calls that overlap on the GPU race, so
- * issue them on one stream. */
+ * first call in each CUDA context (per device: its primary context for runtime
+ * API callers) looks the array up (make it before any stream capture); the
+ * address is cached per context id, so a driver-API context or a context made
+ * after a device reset gets its own lookup.  Calls share the array: calls that
+ * overlap on the GPU race, so issue them on one stream. */
 FP4X_API int llama_attn_decode_bf16_noalloc(fp4x_stream_t stream, uint32_t batch, uint32_t n_heads,
                                             uint32_t n_kv_heads, uint32_t head_dim, uint32_t seq, uint32_t max_seq,
                                             const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
@@ -285,10 +298,14 @@ FP4X_API int llama_model_tp_connect(fp4x_llama_model *m, const void *handles /* 
 FP4X_API int llama_model_shard(const fp4x_llama_model *m, uint32_t *v0, uint32_t *vocab_local);
 FP4X_API int llama_model_get_path(const fp4x_llama_model *m);
 /* Greedy generation as the llama_run loop (llama_run/src/main.rs:544-587, EOS
- * ignored): prefill the prompt one position at a time, then n_gen tokens.
- * prompt/out_ids are HOST arrays; *prefill_ms covers the n_prompt forwards (the
- * last yields the first generated token), *decode_ms the remaining n_gen-1
- * (the reference's timed tokens, :554-562). */
+ * ignored): prefill the prompt, then n_gen tokens.  The prompt is prefilled in
+ * multi-token passes of the batched engine (tcgen05 GEMMs, 64 positions per pass)
+ * straight into the model's KV cache; under tensor parallelism, or with the
+ * environment variable FP4X_PREFILL=serial, it runs one position at a time
+ * through the decode path as the reference does (:550-556).  Either way the last
+ * prompt position yields the first generated token.  prompt/out_ids are HOST
+ * arrays; *prefill_ms covers the prefill, *decode_ms the remaining n_gen-1
+ * tokens (the reference's timed tokens, :554-562). */
 FP4X_API int llama_generate(fp4x_llama_model *m, fp4x_stream_t stream, const uint32_t *prompt, uint32_t n_prompt,
                             uint32_t n_gen, uint32_t *out_ids, float *prefill_ms, float *decode_ms);
 /* Copy one MXFP4 tensor of the model to host in canonical row order (tensor id

@@ -55,3 +55,12 @@ extern "C" int fp4x_device_error(fp4x_stream_t stream, uint32_t *bits_out) {
     }
     return FP4X_OK;
 }
+
+extern "C" int fp4x_set_wait_limit(uint32_t polls) {
+    const cudaError_t e = cudaMemcpyToSymbol(fp4x::g_flag_wait_limit, &polls, sizeof(polls));
+    if (e != cudaSuccess) {
+        fp4x::set_error("fp4x_set_wait_limit: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
+    return FP4X_OK;
+}

@@ -37,6 +37,17 @@ __device__ __forceinline__ void raise_device_error(uint32_t bit) { atomicOr(&g_d
 constexpr uint32_t kSpinLimit = 1u << 21;
 constexpr uint32_t kSuspendHintNs = 1000;
 
+// Poll bound of the waits on flags that ANOTHER rank raises (tensor-parallel
+// exchanges and cross-rank grid barriers); 0 = each wait's compiled default.
+// Set per device by fp4x_set_wait_limit, so that a caller (or a test) can make a
+// wait on a rank that stopped issuing expire in about a millisecond.
+__device__ uint32_t g_flag_wait_limit = 0;
+
+__device__ __forceinline__ uint32_t flag_wait_limit(uint32_t dflt) {
+    const uint32_t v = *(volatile uint32_t *)&g_flag_wait_limit;
+    return v ? v : dflt;
+}
+
 // ---------------------------------------------------------------- smem/mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

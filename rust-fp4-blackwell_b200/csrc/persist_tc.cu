@@ -235,12 +235,13 @@ __device__ bool grid_barrier(Ctx &c) {
             // cross-rank step: CTA 0 tells every rank this rank's grid arrived, waits for
             // all ranks, then releases its own CTAs; epochs keep increasing across launches
             const uint32_t ep = c.epoch0 + c.nbar;
+            const uint32_t lim = flag_wait_limit(kBarLimit);
             if (blockIdx.x == 0) {
                 __threadfence_system();
                 for (uint32_t r = 0; r < p.tp_size; ++r) st_release_sys(p.flagr[r] + 32 * p.tp_rank, ep);
                 for (uint32_t src = 0; src < p.tp_size && ok; ++src)
                     for (uint32_t i = 0; ld_acquire_sys(p.flagr[p.tp_rank] + 32 * src) < ep; ++i)
-                        if (i > kBarLimit || ld_volatile(&p.bar[1])) {
+                        if (i > lim || ld_volatile(&p.bar[1])) {
                             raise_device_error(DEVERR_FLAG_TIMEOUT);
                             ok = 0;
                             break;
@@ -249,8 +250,8 @@ __device__ bool grid_barrier(Ctx &c) {
                 st_release_gpu(&p.bar[2], ok ? ep : 0xFFFFFFFFu);
             } else {
                 for (uint32_t i = 0; ld_acquire(&p.bar[2]) < ep; ++i) {
-                    if (ld_volatile(&p.bar[1]) || i > kBarLimit) {
-                        if (i > kBarLimit) raise_device_error(DEVERR_FLAG_TIMEOUT);
+                    if (ld_volatile(&p.bar[1]) || i > lim) {
+                        if (i > lim) raise_device_error(DEVERR_FLAG_TIMEOUT);
                         ok = 0;
                         break;
                     }

@@ -80,9 +80,10 @@ __device__ bool wait_flags(const uint32_t *flags, uint32_t size, uint32_t epoch)
     if (threadIdx.x == 0) ok = 1;
     __syncthreads();
     if (threadIdx.x < size) {
+        const uint32_t lim = flag_wait_limit(kSpinLimit);
         uint32_t i = 0;
         while (ld_acquire_sys(flags + threadIdx.x) < epoch) {
-            if (++i > kSpinLimit) {
+            if (++i > lim) {
                 raise_device_error(DEVERR_FLAG_TIMEOUT);
                 ok = 0;
                 break;
@@ -273,8 +274,9 @@ __global__ void __launch_bounds__(512) rows_allreduce_kernel(Peers peers, const 
     __syncthreads();
     if (threadIdx.x < size) {
         const uint32_t *f = reinterpret_cast<const uint32_t *>(mine + L.flags) + (phase * kMaxRanks + threadIdx.x) * kRowChunks + c;
+        const uint32_t lim = flag_wait_limit(kSpinLimit);
         for (uint32_t it = 0; ld_acquire_sys(f) < epoch; ++it) {
-            if (it > kSpinLimit) {
+            if (it > lim) {
                 raise_device_error(DEVERR_FLAG_TIMEOUT);
                 ok = 0;
                 break;
@@ -340,8 +342,9 @@ __global__ void __launch_bounds__(1024) rows_argmax_kernel(Peers peers, size_t n
     if (threadIdx.x < size) {
         const uint32_t *f =
             reinterpret_cast<const uint32_t *>(mine + L.aflags) + (size_t)(phase * kMaxRanks + threadIdx.x) * kMaxRows + r;
+        const uint32_t lim = flag_wait_limit(kSpinLimit);
         for (uint32_t it = 0; ld_acquire_sys(f) < epoch; ++it) {
-            if (it > kSpinLimit) {
+            if (it > lim) {
                 raise_device_error(DEVERR_FLAG_TIMEOUT);
                 ok = 0;
                 break;

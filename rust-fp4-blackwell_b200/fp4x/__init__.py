@@ -42,6 +42,7 @@ SIGNATURES = {
     "fp4x_last_error": (C.c_char_p, []),
     "fp4x_version": (C.c_char_p, []),
     "fp4x_device_error": (C.c_int, [_vp, C.POINTER(_u32)]),
+    "fp4x_set_wait_limit": (C.c_int, [_u32]),
     "fp4_quantize_mxfp4": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "fp4_quantize_ref": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "fp4_dequantize_mxfp4": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp]),

@@ -161,3 +161,63 @@ def test_tp2_batched_engine_matches_single_gpu():
     for r, out in res.items():
         assert out["logits_err"] <= 1e-2, (r, out)
         assert out["tokens_equal"], (r, out)
+
+
+def _stall_worker(rank, world, port, cfg, path, result):
+    """Rank 1 stops issuing after one step (it waits on the host, its exchange area
+    still mapped); rank 0 runs one more step with a short flag-wait limit.  The
+    device-side waits for rank 1's flags run out, the kernels return, and rank 0
+    reads FP4X_ETIMEOUT from fp4x_device_error on a context that still works."""
+    import ctypes
+    import datetime
+    import oracle
+    import fp4x
+    from fp4x import Fp4xError, ops, tp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    out = {}
+    L = fp4x.lib()
+    try:
+        toks = oracle.uniform_ids(7, cfg["vocab"], 2)
+        m = tp.create_model(cfg)
+        m.set_path(path)
+        m.forward(int(toks[0]), 0, want_logits=False)  # a normal step on both ranks
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            assert L.fp4x_set_wait_limit(4096) == 0
+            try:
+                m.forward(int(toks[1]), 1, want_logits=False)
+                out["forward"] = "returned"
+            except Fp4xError as e:  # the call may already report the expired wait
+                out["forward"] = str(e)
+            bits = ctypes.c_uint32(0)
+            out["status"] = L.fp4x_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(bits))
+            out["bits"] = bits.value
+            assert L.fp4x_set_wait_limit(0) == 0
+            x = ops.fill_normal(1 << 16, seed=5)
+            torch.cuda.synchronize()
+            out["usable"] = bool(torch.isfinite(x).all().item())
+        dist.barrier()  # rank 1 keeps its area mapped until rank 0's step has ended
+        m.close()
+        torch.cuda.synchronize()
+        result[rank] = out
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("path", ["graph", "tensor"])
+def test_tp2_stalled_rank_wait_expires(path):
+    world = 2
+    with mp.get_context("spawn").Manager() as man:
+        result = man.dict()
+        mp.spawn(_stall_worker, args=(world, _free_port(), TINY, path, result), nprocs=world, join=True)
+        res = dict(result)
+    assert set(res) == {0, 1}
+    r0 = res[0]
+    assert r0["status"] == 3, r0  # FP4X_ETIMEOUT
+    assert r0["bits"] & 2, r0  # DEVERR_FLAG_TIMEOUT
+    assert r0["usable"], r0
