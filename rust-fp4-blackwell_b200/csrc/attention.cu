@@ -705,9 +705,11 @@ extern "C" int llama_attn_decode_f32q_bf16kv(fp4x_stream_t stream, uint32_t batc
 // them the partials live in one file-scope __device__ array of fixed size,
 // kNoAllocScratchFloats floats (4 MiB), which every GPU that loads this library
 // holds until the process exits.  In host code the array's name is only a
-// host-side stand-in, so its device address is looked up once per device with
-// cudaGetSymbolAddress (on the first call made with that device current; make
-// that first call before any stream capture) and cached.
+// host-side stand-in, so its device address is looked up with
+// cudaGetSymbolAddress on the first call made in each CUDA context (the device's
+// primary context for runtime-API callers; make that first call before any
+// stream capture) and cached per context: a caller that switches to another
+// context, or resets the device, gets the address in the context it runs in.
 //
 // All calls share the array and it keeps the last call's contents.  Nothing in
 // it has to start at zero: every slice record a call reads was written earlier
@@ -720,30 +722,66 @@ namespace attn {
 constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-constexpr int kNoAllocMaxDevices = 64;
-static float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+// Addresses already looked up, keyed by the driver's context id (cuCtxGetId: unique
+// for the life of the process, so a context created after a device reset never
+// matches an entry of the one it replaced).
+constexpr int kNoAllocMaxCtx = 64;
+struct NoAllocEntry {
+    unsigned long long id;
+    float *ptr;
+};
+static NoAllocEntry g_noalloc_cache[kNoAllocMaxCtx] = {};
+static int g_noalloc_n = 0, g_noalloc_next = 0;
 static std::mutex g_noalloc_mu;
 
+using PfnCtxGetCurrent = int (*)(void **);
+using PfnCtxGetId = int (*)(void *, unsigned long long *);
+
+// Id of the calling thread's current context; false if there is none (or the
+// driver does not export the calls).
+static bool current_context_id(unsigned long long *id) {
+    static PfnCtxGetCurrent get = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get = reinterpret_cast<PfnCtxGetCurrent>(fn);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PfnCtxGetId>(fn);
+    });
+    void *ctx = nullptr;
+    if (!get || !get_id || get(&ctx) != 0 || ctx == nullptr) return false;
+    return get_id(ctx, id) == 0;
+}
+
 static int noalloc_scratch(float **out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) {
-        set_error("llama_attn_decode_bf16_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    unsigned long long id = 0;
+    bool have_id = current_context_id(&id);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (have_id)
+        for (int i = 0; i < g_noalloc_n; ++i)
+            if (g_noalloc_cache[i].id == id) {
+                *out = g_noalloc_cache[i].ptr;
+                return FP4X_OK;
+            }
+    // first call in this context (for a runtime-API caller with no context yet,
+    // this lookup creates the device's primary context)
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+        set_error("llama_attn_decode_bf16_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
         return FP4X_ECUDA;
     }
-    FP4X_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "llama_attn_decode_bf16_noalloc: device %d out of range",
-                 dev);
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr) {
-            set_error("llama_attn_decode_bf16_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-            return FP4X_ECUDA;
-        }
-        g_noalloc_ptr[dev] = static_cast<float *>(p);
+    if (!have_id) have_id = current_context_id(&id);
+    if (have_id) {  // no id (old driver): look the address up on every call
+        const int slot = g_noalloc_n < kNoAllocMaxCtx ? g_noalloc_n++ : g_noalloc_next++ % kNoAllocMaxCtx;
+        g_noalloc_cache[slot] = {id, static_cast<float *>(p)};
     }
-    *out = g_noalloc_ptr[dev];
+    *out = static_cast<float *>(p);
     return FP4X_OK;
 }
 

@@ -56,8 +56,9 @@ def _close(got, want):
 
 
 def test_noalloc_matches_workspace_entry_point_twice():
-    # two different shapes back to back: both use the split-KV scratch
-    for seed, shape in [(10, (1, 32, 8, 128, 4096)), (20, (4, 32, 4, 64, 2000))]:
+    # different shapes back to back, all on the split-KV scratch: the grouped MMA
+    # kernel (4 and 8 q heads per KV head) and the one-head-per-KV-head kernel
+    for seed, shape in [(10, (1, 32, 8, 128, 4096)), (20, (4, 32, 4, 64, 2000)), (30, (2, 8, 8, 64, 3000))]:
         B, H, NKV, HD, seq = shape
         assert fp4x.lib().llama_attn_workspace_size(B, H, NKV, HD, seq) > 0  # the scratch path is exercised
         q, kc, vc = _case(seed, *shape)
