@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace fp4x {
@@ -48,11 +49,58 @@ bool make_map_sw128(CUtensorMap *map, const void *base, uint64_t row_bytes, uint
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_out(CUtensorMap *map, void *base, uint32_t elem, uint64_t cols, uint64_t rows, uint64_t planes,
+                  uint32_t box_cols, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!encode || (cols * elem) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+    const cuuint64_t dims[3] = {cols, rows, planes};
+    const cuuint64_t strides[2] = {cols * elem, cols * rows * elem};
+    const cuuint32_t box[3] = {box_cols, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return encode(map, elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                  planes > 1 ? 3 : 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace tc
 
 namespace mma {
 
 constexpr int kThreads = 192;
+
+// Per-CTA timestamps (globaltimer, ns) only in builds compiled with
+// -DFP4X_MMA_TIMING; a no-op otherwise.  Slot layout per CTA (linear block id
+// < kMtCtas): 0 start, 1 setup done, 2 + i MMA lane saw stage i (i < 24),
+// 26 last MMA commit, 27 epilogue start, 28 epilogue done, 29 SM id, 30 TMEM
+// reads staged, 31 epilogue warps synchronised.
+#ifdef FP4X_MMA_TIMING
+constexpr uint32_t kMtCtas = 2048, kMtSlots = 32;
+__device__ unsigned long long g_mma_ts[kMtCtas * kMtSlots];
+__device__ __forceinline__ void mts(uint32_t i) {
+    const uint32_t b = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (b < kMtCtas && i < kMtSlots) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_mma_ts[b * kMtSlots + i] = t;
+        if (i == 0) {
+            uint32_t sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            g_mma_ts[b * kMtSlots + 29] = sm;
+        }
+    }
+}
+#else
+__device__ __forceinline__ void mts(uint32_t) {}
+#endif
 constexpr uint32_t kStageK = 256;             // k per stage: one 128-byte swizzle row
 constexpr uint32_t kTileA = 128 * 128;        // weight tile bytes per stage
 constexpr uint32_t kMaxStages = 8;
@@ -67,7 +115,12 @@ enum Mode : uint32_t { OUT_BF16 = 0, OUT_F32 = 1, OUT_ADD_F32 = 2 };
 // row holds 4 blocks = 128 k), 4 for NVFP4 (UE4M3 per 16, an atom row = 64 k).
 struct Geo {
     uint32_t nt, ak, stages, sfb_atoms, stage_bytes, b_off, sfa_off, sfb_off, tmem_cols, sfa_col0, sfb_col0, smem;
+    uint32_t per_sm;  // CTAs resident per SM (2 for tiles of <= 128 tokens: their MMA issue overlaps)
 };
+
+// Two CTAs share an SM when each needs at most half of its shared memory (228 KB,
+// 1 KB reserved per CTA) and half of its 512 tensor-memory columns.
+constexpr uint32_t kSmemHalf = 113 * 1024;
 
 __host__ __device__ inline Geo geometry(uint32_t nt, bool nv = false) {
     Geo g;
@@ -78,15 +131,19 @@ __host__ __device__ inline Geo geometry(uint32_t nt, bool nv = false) {
     g.sfa_off = g.b_off + nt * 128;
     g.sfb_off = g.sfa_off + g.ak * 512;
     g.stage_bytes = (g.sfb_off + g.sfb_atoms * g.ak * 512 + 1023) / 1024 * 1024;
-    uint32_t s = (kSmemLimit - 1024 - kBarBytes) / g.stage_bytes;
-    g.stages = s > kMaxStages ? kMaxStages : s;
-    g.sfa_col0 = nt;
-    g.sfb_col0 = nt + g.stages * 4 * g.ak;
-    const uint32_t cols = g.sfb_col0 + g.stages * 4 * g.ak * g.sfb_atoms;
-    uint32_t c = 32;
-    while (c < cols) c *= 2;
-    g.tmem_cols = c;
-    g.smem = g.stages * g.stage_bytes + 1024 + kBarBytes;
+    for (g.per_sm = nt <= 128 ? 2u : 1u;; g.per_sm = 1) {
+        const uint32_t lim = g.per_sm == 2 ? kSmemHalf : kSmemLimit;
+        uint32_t s = (lim - 1024 - kBarBytes) / g.stage_bytes;
+        g.stages = s > kMaxStages ? kMaxStages : s;
+        g.sfa_col0 = nt;
+        g.sfb_col0 = nt + g.stages * 4 * g.ak;
+        const uint32_t cols = g.sfb_col0 + g.stages * 4 * g.ak * g.sfb_atoms;
+        uint32_t c = 32;
+        while (c < cols) c *= 2;
+        g.tmem_cols = c;
+        g.smem = g.stages * g.stage_bytes + 1024 + kBarBytes;
+        if (g.per_sm == 1 || (g.stages >= 3 && g.tmem_cols <= 256)) break;
+    }
     return g;
 }
 
@@ -103,6 +160,9 @@ struct Args {
     // (scale_image_bytes layouts), loaded per stage by one bulk copy each instead of
     // gathered from sa / sw; both null = gather
     const uint8_t *sa_img, *sw_img;
+    // 1: the epilogue writes its tile with one TMA store (or TMA reduce-add for
+    // OUT_ADD_F32) through map_d; 0: coalesced thread stores
+    uint32_t tma_out;
 };
 
 // Scale-atom image of a [rows][k/32] E8M0 matrix cut into tiles of `tile_rows`
@@ -166,14 +226,35 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ ws, uint32_t spli
     }
 }
 
-// Accumulator -> outputs for the 128 epilogue threads (thread = weight row
-// row0 + 32q + lane; TMEM lane quarter q).  Column c of the tile is A row tok0 + c;
-// T consecutive columns are the terms of one token and are added.  With split K
-// the sums go to this split's partial slice.
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void sts_b16(uint32_t addr, uint16_t v) {
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Accumulator -> outputs for the 128 epilogue threads (thread t: TMEM lane
+// quarter q = warp % 4, tile row 32q + lane).  Column c of the tile is A row
+// tok0 + c; T consecutive columns are the terms of one token and are added.
+// The tile goes through shared memory (the stage buffers, idle once the last
+// MMA has completed) as [token][128 rows] of the output type, and leaves with
+// one TMA tile store (a TMA reduce-add for OUT_ADD_F32; the box is clipped at
+// the tensor's edges), or -- when the output rows are not 16-byte granular --
+// f32 staging and coalesced thread stores.  Writing straight from TMEM (one
+// 2-byte store per element) took half of a CTA's lifetime at 256 tokens.  With
+// split K the sums go to this split's partial slice.
 template <uint32_t T>
-__device__ void epilogue_sums(const Args &a, uint32_t tbase, uint32_t q, uint32_t row, uint32_t tok0) {
-    const bool row_ok = row < a.n;
-    const uint32_t tokens = a.m / T;
+__device__ void epilogue_tile(const Args &a, const CUtensorMap *map_d, uint32_t tbase, uint32_t q, uint32_t lane,
+                              uint32_t t, uint32_t row0, uint32_t tok0, uint8_t *stg) {
+    const uint32_t r = 32 * q + lane, ntok = a.nt / T, tokens = a.m / T, tk0 = tok0 / T;
+    const bool bf = a.tma_out && a.splits == 1 && a.mode == OUT_BF16;  // bf16 staging image
+    const uint32_t sbase = smem_u32(stg);
     for (uint32_t c0 = 0; c0 < a.nt; c0 += 32) {
         float v[4][8];
 #pragma unroll
@@ -188,13 +269,60 @@ __device__ void epilogue_sums(const Args &a, uint32_t tbase, uint32_t q, uint32_
                 float sum = v[u][j];
 #pragma unroll
                 for (uint32_t e = 1; e < T; ++e) sum += v[u][j + e];
-                sum *= a.alpha;
-                const uint32_t tk = (tok0 + c0 + 8 * u + j) / T;
-                if (!row_ok || tk >= tokens) continue;
-                if (a.splits > 1)
-                    a.ws[((size_t)blockIdx.z * tokens + tk) * a.n + row] = sum;
+                const uint32_t idx = ((c0 + 8 * u + j) / T) * 128 + r;
+                if (bf)
+                    sts_b16(sbase + 2 * idx, f32_to_bf16_bits(sum * a.alpha));
                 else
-                    emit(a, tk, row, sum);
+                    sts_f32(sbase + 4 * idx, sum * a.alpha);
+            }
+        }
+    }
+    if (a.tma_out) {
+        fence_proxy_async_smem();  // this thread's staging writes -> the TMA engine
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (t == 0) {
+            if (a.splits > 1)
+                tc::tma_store_3d(map_d, (int32_t)row0, (int32_t)tk0, (int32_t)blockIdx.z, stg);
+            else if (a.mode == OUT_ADD_F32)
+                tc::tma_reduce_add_2d(map_d, (int32_t)row0, (int32_t)tk0, stg);
+            else
+                tc::tma_store_2d(map_d, (int32_t)row0, (int32_t)tk0, stg);
+            tc::bulk_commit();
+            tc::bulk_wait_all();
+        }
+        return;
+    }
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+    const uint32_t rows = a.n - row0 < 128u ? a.n - row0 : 128u;
+    const bool vec = (a.n & 3u) == 0 && rows == 128;
+    for (uint32_t i = t; i < ntok * 32; i += 128) {
+        const uint32_t tk = i / 32, c4 = i % 32, tok = tk0 + tk;
+        if (tok >= tokens) continue;
+        const float4 v = lds_f32x4(sbase + 16 * i);
+        const uint32_t row = row0 + 4 * c4;
+        const size_t o = (size_t)tok * a.n + row;
+        if (vec && a.splits > 1) {
+            *reinterpret_cast<float4 *>(a.ws + (size_t)blockIdx.z * tokens * a.n + o) = v;
+        } else if (vec && a.mode == OUT_BF16) {
+            const uint32_t lo = (uint32_t)f32_to_bf16_bits(v.x) | ((uint32_t)f32_to_bf16_bits(v.y) << 16);
+            const uint32_t hi = (uint32_t)f32_to_bf16_bits(v.z) | ((uint32_t)f32_to_bf16_bits(v.w) << 16);
+            *reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(a.d) + o) = make_uint2(lo, hi);
+        } else if (vec && a.mode == OUT_F32) {
+            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.d) + o) = v;
+        } else if (vec) {  // OUT_ADD_F32: one writer per element
+            float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.d) + o);
+            float4 x = *p;
+            x.x += v.x, x.y += v.y, x.z += v.z, x.w += v.w;
+            *p = x;
+        } else {
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                if (4 * c4 + k >= rows) break;
+                if (a.splits > 1)
+                    a.ws[(size_t)blockIdx.z * tokens * a.n + o + k] = e[k];
+                else
+                    emit(a, tok, row + k, e[k]);
             }
         }
     }
@@ -240,7 +368,8 @@ __device__ __forceinline__ uint4 load_scales16(const uint8_t *s, uint32_t row, u
 // NV: NVFP4 operands (UE4M3 scales per 16, kind::mxf4nvf4); otherwise MXFP4.
 template <bool NV>
 __global__ void __launch_bounds__(kThreads, 1)
-    mxf4_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a, Args a) {
+    mxf4_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_d, Args a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Geo G = geometry(a.nt, NV);
@@ -253,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint32_t *abort = tmem_slot + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) mts(0);
     const uint32_t tok0 = blockIdx.x * a.nt, row0 = blockIdx.y * 128;
     const uint32_t kst = (a.k + kStageK - 1) / kStageK, kbt = a.k / (NV ? 16 : 32);
     const uint32_t s0 = blockIdx.z * a.kps, s1 = min(kst, s0 + a.kps);
@@ -282,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tbase = *tmem_slot;
+    if (threadIdx.x == 0) mts(1);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -316,6 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t slot = i % S, par = (i / S) & 1;
                 if (!wait_or_abort(&full_t[slot], par, abort) || (!pre && !wait_or_abort(&full_s[slot], par, abort)))
                     break;
+                mts(2 + i);
                 tc::fence_after_sync();
                 const uint8_t *st = smem + slot * G.stage_bytes;
                 const uint32_t sa_col = tbase + G.sfa_col0 + slot * 4 * G.ak;
@@ -340,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc::commit(&empty[slot]);
             }
+            mts(26);
             tc::commit(accb);  // also on abort: the epilogue then knows no MMA is in flight
         }
     } else {
@@ -389,12 +522,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = wait_or_abort(accb, 0, abort);
         ok = __all_sync(0xffffffffu, ok);
         tc::fence_after_sync();
-        const uint32_t q = (uint32_t)warp & 3, row = row0 + 32 * q + lane;
+        // one decision for the 4 epilogue warps (the tile epilogue synchronises them)
+        if (!ok && lane == 0) *abort = 1;
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        ok = *abort == 0;
+        if (t == 0) mts(27);
+        const uint32_t q = (uint32_t)warp & 3;
+        uint8_t *stg = smem;  // stage buffers: every TMA copy and MMA has completed
         if (ok) {
-            if (a.terms == 8) epilogue_sums<8>(a, tbase, q, row, tok0);
-            else if (a.terms == 4) epilogue_sums<4>(a, tbase, q, row, tok0);
-            else epilogue_sums<1>(a, tbase, q, row, tok0);
+            if (a.terms == 8) epilogue_tile<8>(a, &map_d, tbase, q, lane, t, row0, tok0, stg);
+            else if (a.terms == 4) epilogue_tile<4>(a, &map_d, tbase, q, lane, t, row0, tok0, stg);
+            else epilogue_tile<1>(a, &map_d, tbase, q, lane, t, row0, tok0, stg);
         }
+        if (t == 0) mts(28);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -477,10 +617,11 @@ inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true, bo
     p.m_tiles = (m + p.nt - 1) / p.nt;
     p.n_tiles = (n + 127) / 128;
     p.kst = (k + kStageK - 1) / kStageK;
-    const uint32_t tiles = p.m_tiles * p.n_tiles, sms = (uint32_t)num_sms();
-    // One CTA per SM: time ~ waves x (stages per CTA + ~2 stages of pipeline fill
-    // and epilogue).  Take the fewest splits that reach the minimum (each split
-    // adds an fp32 partial per output).
+    p.g = geometry(p.nt, nv);
+    const uint32_t tiles = p.m_tiles * p.n_tiles, sms = (uint32_t)num_sms() * p.g.per_sm;
+    // Time ~ waves x (stages per CTA + ~2 stages of pipeline fill and epilogue),
+    // a wave being every CTA slot of the GPU.  Take the fewest splits that reach
+    // the minimum (each split adds an fp32 partial per output).
     uint32_t splits = 1, best = ~0u;
     for (uint32_t s = 1; s <= (allow_split ? std::min(p.kst, 16u) : 1u); ++s) {
         const uint32_t waves = (tiles * s + sms - 1) / sms, per = (p.kst + s - 1) / s;
@@ -489,7 +630,6 @@ inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true, bo
     }
     p.kps = (p.kst + splits - 1) / splits;
     p.splits = (p.kst + p.kps - 1) / p.kps;
-    p.g = geometry(p.nt, nv);
     return p;
 }
 
@@ -534,12 +674,29 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
         set_error("fp4_mma: split-K launch without a workspace");
         return FP4X_EINVAL;
     }
-    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials, alpha, sa_img, sw_img};
+    if ((size_t)p.g.stages * p.g.stage_bytes < (size_t)p.nt * 128 * sizeof(float)) {  // epilogue staging tile
+        set_error("fp4_mma: %u-token tile does not fit the epilogue staging area", p.nt);
+        return FP4X_EUNSUPPORTED;
+    }
+    Args args{m, n, k, p.nt, p.kps, sa, sw, d, (uint32_t)mode, terms, p.splits, partials, alpha, sa_img, sw_img, 0};
+    // output tile stores by TMA where the rows are 16-byte granular (the map encoder
+    // checks the base alignment); otherwise coalesced thread stores
+    CUtensorMap map_d;
+    memset(&map_d, 0, sizeof(map_d));
+    {
+        const uint32_t tokens = m / terms, box_rows = p.nt / terms;
+        bool ok;
+        if (p.splits > 1)
+            ok = tc::make_map_out(&map_d, partials, 4, n, tokens, p.splits, 128, box_rows);
+        else
+            ok = tc::make_map_out(&map_d, d, mode == OUT_BF16 ? 2 : 4, n, tokens, 1, 128, box_rows);
+        args.tma_out = ok ? 1u : 0u;
+    }
     const dim3 grid(p.m_tiles, p.n_tiles, p.splits);
     if (nv)
-        mxf4_gemm_kernel<true><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, args);
+        mxf4_gemm_kernel<true><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, map_d, args);
     else
-        mxf4_gemm_kernel<false><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, args);
+        mxf4_gemm_kernel<false><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, map_d, args);
     if (p.splits > 1) {
         const size_t total = (size_t)(m / terms) * n;
         const uint32_t blocks = (uint32_t)std::min<size_t>((total / 4 + 255) / 256 + 1, 8u * (uint32_t)num_sms());
@@ -606,6 +763,18 @@ extern "C" int fp4_mma_nvf4_f32(fp4x_stream_t stream, uint32_t m, uint32_t n, ui
     return mma::launch((cudaStream_t)stream, m, n, k, a, a_scales, w, w_scales, d, mma::OUT_F32, p, 1, nullptr, true,
                        alpha);
 }
+
+#ifdef FP4X_MMA_TIMING
+extern "C" FP4X_API int fp4x_mma_timestamps(unsigned long long *out, uint32_t n) {
+    if (n == 0) {  // reset
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, mma::g_mma_ts) != cudaSuccess) return 2;
+        return cudaMemset(p, 0, sizeof(mma::g_mma_ts)) == cudaSuccess ? 0 : 2;
+    }
+    n = std::min<uint32_t>(n, mma::kMtCtas * mma::kMtSlots);
+    return cudaMemcpyFromSymbol(out, mma::g_mma_ts, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : 2;
+}
+#endif
 
 extern "C" int fp4_mma_allones(fp4x_stream_t stream, float *out) {
     FP4X_REQUIRE(out, "fp4_mma_allones: null pointer");

@@ -139,6 +139,30 @@ __device__ __forceinline__ void tma_load_2d(void *dst_smem, const CUtensorMap *m
         : "memory");
 }
 
+// Tile stores shared -> global (bulk async-group of the issuing thread).  The box
+// is written where it lies inside the tensor; parts outside it are dropped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int32_t x, int32_t y, const void *src_smem) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src_smem))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
+                                             const void *src_smem) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(smem_u32(src_smem))
+                 : "memory");
+}
+// Element-wise add of the box into global memory (performed by the L2).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, int32_t x, int32_t y,
+                                                  const void *src_smem) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src_smem))
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -151,6 +175,13 @@ __host__ __device__ constexpr uint32_t scale_atom_off(uint32_t r, uint32_t j) {
 // Host: 2-D row-major byte matrix [rows][pitch] as a tensor map with a
 // 128-byte x box_rows box and the 128-byte swizzle.  Returns false on failure.
 bool make_map_sw128(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows);
+
+// Host: output tensor [planes][rows][cols] of bf16 (elem 2) or f32 (elem 4),
+// row-major, as a tensor map with a box of box_cols x box_rows (x 1 plane), no
+// swizzle: the shared-memory image of a box is [box_rows][box_cols].  cols x elem
+// must be a multiple of 16.  Returns false on failure.
+bool make_map_out(CUtensorMap *map, void *base, uint32_t elem, uint64_t cols, uint64_t rows, uint64_t planes,
+                  uint32_t box_cols, uint32_t box_rows);
 
 // Bulk reduction of `bytes` (multiple of 16) of f32 from shared memory into global
 // memory (element-wise add, performed by the L2 a sector at a time), tracked by
