@@ -364,11 +364,10 @@ int build_persistent(fp4x_llama_model *m, const ptc::TpIn *tpin) {
             rc = trc;
         }
     }
-    // Under tensor parallelism the graph path (per-layer kernels + the peer-memory
-    // allreduce kernel) is the default: the fused tensor kernel makes every grid
-    // barrier cross-rank and measured slower there (8B shape, 4096 context: 3.67 ms per
-    // token at 2 ranks, 4.71 ms at 4, against 2.26 ms for the graph path at 4).
-    if (tpin) m->path = 0;
+    // Under tensor parallelism the tensor-core kernel is the default too (its grid
+    // barriers stay on one GPU; ranks meet only in the row-parallel exchanges after
+    // the O and down projections and at the argmax); the graph path (per-layer
+    // kernels + the peer-memory allreduce kernel) remains selectable.
     const char *env = getenv("FP4X_DECODE_PATH");
     if (env && strcmp(env, "graph") == 0) m->path = 0;
     if (env && strcmp(env, "persistent") == 0 && m->pe) m->path = 1;

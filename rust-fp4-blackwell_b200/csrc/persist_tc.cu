@@ -39,10 +39,11 @@ namespace ptc {
 constexpr uint32_t kBarLimit = 1u << 24;
 
 // Timestamps (globaltimer, ns) of CTA 0 and the last CTA, only in builds
-// compiled with -DFP4X_PHASE_TIMING; a no-op otherwise.  Slot = 24 per layer
-// (and 32 for the lm_head) per token: consumer steps 0..18, MMA lane 19..23,
-// operand build split (decomposition done / fence done) 24..31.
-constexpr uint32_t kTsPerLayer = 32;
+// compiled with -DFP4X_PHASE_TIMING; a no-op otherwise.  kTsPerLayer slots per
+// layer (and the lm_head) per token: consumer steps 0..18, MMA lane 19..23,
+// operand build split (decomposition done / fence done) 24..31, split-attention
+// unit steps 32..34 (q staged, warp 0's positions done, warps merged).
+constexpr uint32_t kTsPerLayer = 40;
 #ifdef FP4X_PHASE_TIMING
 constexpr uint32_t kTcStamps = 1u << 15;
 __device__ unsigned long long g_tc_ts[2][kTcStamps];
@@ -144,9 +145,6 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t *p) {
 __device__ __forceinline__ void red_add(float *p, float v) {
     asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
-__device__ __forceinline__ void red_add_sys(float *p, float v) {
-    asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
-}
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -157,15 +155,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 }
 __device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// A row-parallel output element: added into this rank's buffer, and under tensor
-// parallelism into every rank's (peer memory over NVLink).
-__device__ __forceinline__ void add_all_ranks(float *const *bufs, uint32_t ranks, uint32_t i, float v) {
-    if (ranks == 1) {
-        red_add(bufs[0] + i, v);
-    } else {
-        for (uint32_t r = 0; r < ranks; ++r) red_add_sys(bufs[r] + i, v);
-    }
 }
 
 // Bounded mbarrier wait that also gives up when the launch has aborted.
@@ -192,21 +181,24 @@ struct Ctx {
     uint32_t nbar;
     uint32_t tsb;  // timestamp slot base of the current layer
     uint32_t epoch0;  // cross-rank barrier epochs before this launch
+    uint32_t xn;      // row-parallel exchanges of each kind done (tensor parallel)
     bool ok;
 };
 
 // All consumer threads call this; a failed wait earlier only marks the context,
-// so the decision to stop is CTA-uniform here.
-__device__ bool grid_barrier(Ctx &c) {
+// so the decision to stop is CTA-uniform here.  With `cross` (and more than one
+// rank) the barrier spans every rank's grid; otherwise it is this GPU's grid.
+__device__ bool grid_barrier(Ctx &c, bool cross = false) {
     const Params &p = *c.p;
+    const bool xrank = cross && p.tp_size > 1;
     volatile uint32_t *flag = reinterpret_cast<volatile uint32_t *>(c.smem + c.L.flag);
     if (!c.ok) flag[1] = 1;
     csync();
     c.nbar += 1;
     if (threadIdx.x == 0) {
         if (flag[1]) atomicExch(&p.bar[1], 1u);
-        if (p.tp_size > 1) {
-            __threadfence_system();  // this CTA's adds into peer memory are visible before it arrives
+        if (xrank) {
+            __threadfence_system();  // this CTA's writes into peer memory are visible before it arrives
             atomicAdd(&p.bar[0], 1u);
         } else {
             // release: the CTA's writes (ordered before this thread by the CTA barrier)
@@ -231,7 +223,7 @@ __device__ bool grid_barrier(Ctx &c) {
             }
             __nanosleep(32);
         }
-        if (ok && p.tp_size > 1) {
+        if (ok && xrank) {
             // cross-rank step: CTA 0 tells every rank this rank's grid arrived, waits for
             // all ranks, then releases its own CTAs; epochs keep increasing across launches
             const uint32_t ep = c.epoch0 + c.nbar;
@@ -261,12 +253,92 @@ __device__ bool grid_barrier(Ctx &c) {
         }
         // one GPU: the acquire load above already orders this CTA's later reads (the
         // CTA barrier below passes that on); the cross-rank path keeps its fence
-        if (p.tp_size > 1) __threadfence();
+        if (xrank) __threadfence();
         flag[0] = ok;
         if (!ok) *c.B.abort = 1;
     }
     csync();
     c.ok = flag[0] != 0;
+    return c.ok;
+}
+
+// Row-parallel reduction under tensor parallelism (kind 0: the O-projection
+// partials in tpo, 1: the down-projection partials in tpd), added into X.  CTA i
+// owns slice i of the vector on every rank: each of its threads pushes one
+// element of this rank's partial into every peer's receive slot as a 64-bit word
+// {value, tag} (a single-copy-atomic store over NVLink, tag = n + 1), clears the
+// element of the partial, then polls its own slots until every peer's word carries
+// the tag and adds the ranks' values in rank order (the same bits on every rank).
+// The tag makes each word self-validating, so no fence or flag orders the data.
+// `n` numbers the exchanges of a kind (slot parity n & 1: a rank reaches exchange
+// n + 2 of a kind only after every rank has finished exchange n, through the
+// exchanges in between); a local grid barrier must follow before X is read.
+// llama_run/src/main.rs:522-530 with the contraction split across ranks.
+__device__ bool tp_exchange(Ctx &c, uint32_t kind, uint32_t n) {
+    const Params &p = *c.p;
+    const uint32_t T = p.tp_size, me = p.tp_rank, dim = p.dim, par = n & 1u, tag = n + 1;
+    const uint32_t per = ((dim + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+    const uint32_t e0 = min(dim, blockIdx.x * per), e1 = min(dim, e0 + per);
+    float *part = kind ? p.tpd : p.tpo;
+    volatile uint32_t *flag = reinterpret_cast<volatile uint32_t *>(c.smem + c.L.flag);
+    float own[2] = {0.f, 0.f};  // per <= 2 * kCons: dim <= 2 * kCons * grid
+#pragma unroll
+    for (uint32_t u = 0; u < 2; ++u) {
+        const uint32_t i = e0 + threadIdx.x + u * kCons;
+        if (i < e1) {
+            own[u] = __ldcg(part + i);
+            part[i] = 0.0f;
+            const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(own[u]);
+            for (uint32_t r = 0; r < T; ++r)
+                if (r != me) {
+                    uint64_t *dst = (kind ? p.trd[r] : p.tro[r]) + ((size_t)par * kMaxTp + me) * dim + i;
+                    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+                }
+        }
+    }
+    const uint64_t *recv = kind ? p.trd[me] : p.tro[me];
+    const uint32_t lim = flag_wait_limit(kBarLimit);
+    bool ok = c.ok;
+#pragma unroll
+    for (uint32_t u = 0; u < 2; ++u) {
+        const uint32_t i = e0 + threadIdx.x + u * kCons;
+        if (i >= e1 || !ok) continue;
+        // every peer's word is loaded at once; the ones without the tag are polled again
+        uint64_t w[kMaxTp] = {};
+        uint32_t pending = ((1u << T) - 1u) & ~(1u << me);
+        for (uint32_t it = 0; pending; ++it) {
+#pragma unroll
+            for (uint32_t r = 0; r < kMaxTp; ++r)
+                if ((pending >> r) & 1u)
+                    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];"
+                                 : "=l"(w[r])
+                                 : "l"(recv + ((size_t)par * kMaxTp + r) * dim + i)
+                                 : "memory");
+#pragma unroll
+            for (uint32_t r = 0; r < kMaxTp; ++r)
+                if (((pending >> r) & 1u) && (uint32_t)(w[r] >> 32) == tag) pending &= ~(1u << r);
+            if (pending && (((it & 63) == 63 && ld_volatile(&p.bar[1])) || it > lim)) {
+                if (it > lim) {
+                    raise_device_error(DEVERR_FLAG_TIMEOUT);
+                    atomicExch(&p.bar[1], 1u);
+                }
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) continue;
+        float acc = 0.0f;
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxTp; ++r)
+            if (r < T) acc += r == me ? own[u] : __uint_as_float((uint32_t)w[r]);
+        p.X[i] = __ldcg(p.X + i) + acc;  // this CTA alone writes its slice
+    }
+    if (threadIdx.x == 0) flag[2] = 1;
+    csync();
+    if (!ok) flag[2] = 0;
+    csync();
+    c.ok = flag[2] != 0;
+    if (!c.ok && threadIdx.x == 0) *c.B.abort = 1;
     return c.ok;
 }
 
@@ -529,6 +601,8 @@ __device__ void phase_qkv(Ctx &c, uint32_t l, uint32_t tok, uint32_t lay_count) 
     const Sched &S = *c.S;
     if (l == 0)
         norm_decompose<2>(c, p.embed + (size_t)tok * p.dim, p.attn_norm, S.n_a > 0);
+    else if (p.tp_size > 1)  // the exchanges have already added every partial into X
+        norm_decompose<0>(c, nullptr, p.attn_norm + (size_t)l * p.dim, S.n_a > 0);
     else
         norm_decompose<1>(c, nullptr, p.attn_norm + (size_t)l * p.dim, S.n_a > 0);
     CST(1);
@@ -700,6 +774,7 @@ __device__ void attend(Ctx &c, uint32_t l, uint32_t pos) {
 // Fold the previous layer's FFN delta into X (a slice per CTA) and clear it.
 __device__ void fold_delta(Ctx &c, uint32_t l) {
     const Params &p = *c.p;
+    if (p.tp_size > 1) return;  // tensor parallel: the down exchange adds into X itself
     const uint32_t per = (p.dim + gridDim.x - 1) / gridDim.x;
     const uint32_t e0 = blockIdx.x * per, e1 = min(p.dim, e0 + per);
     for (uint32_t e = e0 + threadIdx.x; e < e1; e += kCons) {
@@ -726,7 +801,8 @@ __device__ void o_projection(Ctx &c, uint32_t lay_count, int fold_l = -1) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (uint32_t i = warp >> 2; i < S.n_pairs; i += kCW / 4) {
         const float s = acc_row(c.tbase, 8 * i);
-        add_all_ranks(p.xr, p.tp_size, S.pair_tile[i] * 128 + 32 * (warp & 3) + lane, s);
+        const uint32_t row = S.pair_tile[i] * 128 + 32 * (warp & 3) + lane;
+        red_add((p.tp_size > 1 ? p.tpo : p.X) + row, s);  // this rank's partial under TP
     }
     CST(10);
 }
@@ -792,6 +868,7 @@ __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
         vb[(size_t)pos * row + j + half] = f32_to_bf16_bits(__ldcg(vr + j + half));
     }
     csync();
+    CST(32);
     float *ps = reinterpret_cast<float *>(c.smem + c.L.ps) + warp * (kMaxGroup * 32);
     float m[GRP], lsum[GRP], o[GRP][NV];
 #pragma unroll
@@ -859,6 +936,7 @@ __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
         }
         __syncwarp();
     }
+    CST(33);
     // merge the warps per head (fixed order), one head at a time through wst
     float *wst = reinterpret_cast<float *>(c.smem + c.L.wst);  // [kCW][HD + 2]
 #pragma unroll 1
@@ -898,6 +976,7 @@ __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
         }
         csync();
     }
+    CST(34);
 }
 
 // Split attention, part 1 (every CTA): fold the FFN delta, then this CTA's unit.
@@ -923,22 +1002,48 @@ __device__ void phase_attn_combine_o(Ctx &c, uint32_t lay_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
     if (S.n_pairs == 0) return;
-    const uint32_t hd = p.hd, slices = p.attn_slices;
+    const uint32_t hd = p.hd, NS = p.attn_slices, nh = S.nh, tid = threadIdx.x;
+    const uint32_t warp = tid >> 5, lane = tid & 31;
     float *xv = reinterpret_cast<float *>(c.smem + c.L.xv);
-    for (uint32_t i = threadIdx.x; i < S.nh * hd; i += kCons) {
-        const uint32_t hs = i / hd, d = i % hd;
-        const float *rec = p.attn_part + (size_t)(S.h0 + hs) * slices * (hd + 2);
+    // the split-attention probability area is free here: [nh][NS] slice maxima (then
+    // their factors), [nh][NS] slice sums, [G][nh * hd] partial outputs
+    float *fm = reinterpret_cast<float *>(c.smem + c.L.ps), *fl = fm + nh * NS, *part = fl + nh * NS;
+    auto rec = [&](uint32_t hs, uint32_t s) { return p.attn_part + ((size_t)(S.h0 + hs) * NS + s) * (hd + 2); };
+    for (uint32_t i = tid; i < nh * NS; i += kCons) {
+        const float *r = rec(i / NS, i % NS);
+        fm[i] = __ldcg(r);
+        fl[i] = __ldcg(r + 1);
+    }
+    csync();
+    if (warp < nh) {  // warp hs: the head's maximum, slice factors and normaliser
         float M = -INFINITY;
-        for (uint32_t s = 0; s < slices; ++s) M = fmaxf(M, __ldcg(rec + s * (hd + 2)));
-        float L = 0.0f, O = 0.0f;
-        for (uint32_t s = 0; s < slices; ++s) {
-            const float ms = __ldcg(rec + s * (hd + 2));
-            if (ms == -INFINITY) continue;
-            const float f = __expf(ms - M);
-            L += __ldcg(rec + s * (hd + 2) + 1) * f;
-            O += __ldcg(rec + s * (hd + 2) + 2 + d) * f;
+        for (uint32_t s = lane; s < NS; s += 32) M = fmaxf(M, fm[warp * NS + s]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (uint32_t s = lane; s < NS; s += 32) {
+            const float ms = fm[warp * NS + s];
+            const float f = ms == -INFINITY ? 0.0f : __expf(ms - M);
+            fm[warp * NS + s] = f;
+            L += fl[warp * NS + s] * f;
         }
-        xv[i] = O / L;
+        L = warp_sum(L);
+        if (lane == 0) c.red[warp] = L;
+    }
+    csync();
+    // G slice groups per output column, each summing its slices with independent loads
+    const uint32_t cols = nh * hd, G = max(1u, min(kCons / cols, NS));
+    for (uint32_t i = tid; i < G * cols; i += kCons) {
+        const uint32_t g = i / cols, col = i % cols, hs = col / hd, d = col % hd;
+        float O = 0.0f;
+#pragma unroll 4
+        for (uint32_t s2 = g; s2 < NS; s2 += G) O += fm[hs * NS + s2] * __ldcg(rec(hs, s2) + 2 + d);
+        part[i] = O;
+    }
+    csync();
+    for (uint32_t i = tid; i < cols; i += kCons) {
+        float O = 0.0f;
+        for (uint32_t g = 0; g < G; ++g) O += part[g * cols + i];
+        xv[i] = O / c.red[i / hd];
     }
     csync();
     CST(7);
@@ -986,28 +1091,21 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     CST(16);
     if (!c.ok) return;
     const uint32_t mt = p.dim / 128;
-    if (p.tp_size == 1) {
-        // The CTA's whole down partial (dim values) is added into Y by one bulk
-        // reduction: the L2 applies it a sector at a time instead of one element
-        // per red.add (148 CTAs x dim element updates per layer otherwise).  The
-        // staging buffer (the activation staging area, free once the down MMAs
-        // are done) is read by the bulk copy before this thread reaches the next
-        // grid barrier.
-        float *stg = reinterpret_cast<float *>(c.smem + c.L.xv);
-        for (uint32_t t = warp >> 2; t < mt; t += kCW / 4)
-            stg[t * 128 + 32 * (warp & 3) + lane] = acc_row(c.tbase, 8 * t);
-        fence_proxy_async_smem();
-        csync();
-        if (threadIdx.x == 0) {
-            tc::bulk_reduce_add_f32(p.Y, stg, p.dim * 4);
-            tc::bulk_commit();
-            tc::bulk_wait_all();
-        }
-    } else {
-        for (uint32_t t = warp >> 2; t < mt; t += kCW / 4) {
-            const float s = acc_row(c.tbase, 8 * t);
-            add_all_ranks(p.yr, p.tp_size, t * 128 + 32 * (warp & 3) + lane, s);
-        }
+    // The CTA's whole down partial (dim values) is added into Y (this rank's partial
+    // accumulator under TP) by one bulk reduction: the L2 applies it a sector at a
+    // time instead of one element per red.add (148 CTAs x dim element updates per
+    // layer otherwise).  The staging buffer (the activation staging area, free once
+    // the down MMAs are done) is read by the bulk copy before this thread reaches
+    // the next grid barrier.
+    float *stg = reinterpret_cast<float *>(c.smem + c.L.xv);
+    for (uint32_t t = warp >> 2; t < mt; t += kCW / 4)
+        stg[t * 128 + 32 * (warp & 3) + lane] = acc_row(c.tbase, 8 * t);
+    fence_proxy_async_smem();
+    csync();
+    if (threadIdx.x == 0) {
+        tc::bulk_reduce_add_f32(p.tp_size > 1 ? p.tpd : p.Y, stg, p.dim * 4);
+        tc::bulk_commit();
+        tc::bulk_wait_all();
     }
     CST(17);
 }
@@ -1016,7 +1114,10 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
 __device__ void phase_lm(Ctx &c, uint32_t tok_count) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
-    norm_decompose<1>(c, nullptr, p.final_norm, S.n_l > 0);
+    if (p.tp_size > 1)
+        norm_decompose<0>(c, nullptr, p.final_norm, S.n_l > 0);
+    else
+        norm_decompose<1>(c, nullptr, p.final_norm, S.n_l > 0);
     CST(1);
     float bv = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
@@ -1290,6 +1391,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
         c.red = reinterpret_cast<float *>(smem + L.red);
         c.nbar = 0, c.ok = true;
         c.epoch0 = p.tp_size > 1 ? *p.epoch : 0u;
+        c.xn = p.tp_size > 1 ? *p.xepoch : 0u;
         uint32_t tok = p.state[0], pos = pos0;
         const uint32_t n_prompt = p.state[3], cap = p.state[4];
         for (uint32_t it = 0; it < n_eff && c.ok; ++it) {
@@ -1308,16 +1410,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
                     phase_attn_o(c, l, pos, lc);
                 }
                 if (!grid_barrier(c)) break;
+                if (p.tp_size > 1 && (!tp_exchange(c, 0, c.xn) || !grid_barrier(c))) break;
                 CST(11);
                 phase_ffn(c, l, lc);
                 if (!grid_barrier(c)) break;
+                if (p.tp_size > 1 && (!tp_exchange(c, 1, c.xn) || !grid_barrier(c))) break;
+                c.xn += 1;
                 CST(18);
             }
             if (!c.ok) break;
             c.tsb = (it * (p.n_layers + 1) + p.n_layers) * kTsPerLayer;
             CST(0);
             phase_lm(c, it);
-            if (!grid_barrier(c)) break;
+            if (!grid_barrier(c, true)) break;  // every rank's argmax candidates are in place
             CST(5);
             // every CTA reduces the candidates itself (same order -> same token)
             float *rv = c.red;
@@ -1356,7 +1461,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
             atomicExch(&p.bar[1], 1u);
         }
         // every rank ran the same barrier sequence: record it for the next launch
-        if (p.tp_size > 1 && c.ok && blockIdx.x == 0 && threadIdx.x == 0) *p.epoch = c.epoch0 + c.nbar;
+        if (p.tp_size > 1 && c.ok && blockIdx.x == 0 && threadIdx.x == 0) {
+            *p.epoch = c.epoch0 + c.nbar;
+            *p.xepoch = c.xn;
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -1473,6 +1581,10 @@ struct TpIn {
     float *xr[kMaxTp] = {}, *yr[kMaxTp] = {}, *cvr[kMaxTp] = {};
     uint32_t *cir[kMaxTp] = {}, *flagr[kMaxTp] = {};
     uint32_t *epoch = nullptr;
+    // row-parallel exchange: every rank's receive slots, this rank's partials
+    uint64_t *ro[kMaxTp] = {}, *rd[kMaxTp] = {};
+    float *po = nullptr, *pd = nullptr;
+    uint32_t *xepoch = nullptr;
 };
 
 #define PTC_UNSUPPORTED(...)            \
@@ -1775,7 +1887,9 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
         for (uint32_t r = 0; r < tpin->size; ++r) {
             P.xr[r] = tpin->xr[r], P.yr[r] = tpin->yr[r], P.cvr[r] = tpin->cvr[r], P.cir[r] = tpin->cir[r];
             P.flagr[r] = tpin->flagr[r];
+            P.tro[r] = tpin->ro[r], P.trd[r] = tpin->rd[r];
         }
+        P.tpo = tpin->po, P.tpd = tpin->pd, P.xepoch = tpin->xepoch;
     }
     P.state = in.state, P.prompt = in.prompt, P.out = in.out, P.bar = bar, P.n_tokens = 0;
     e->p = P;

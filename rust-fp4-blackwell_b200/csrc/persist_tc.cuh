@@ -104,6 +104,15 @@ struct Params {
     uint32_t *cir[kMaxTp];                     // ... and indices
     uint32_t *flagr[kMaxTp];                   // every rank's barrier flags, one 32-word line per source rank
     uint32_t *epoch;                           // cross-rank barrier epochs done so far (kept across launches)
+    // Row-parallel exchange (tp_size > 1): the O and down partials are added into this
+    // rank's own accumulators tpo / tpd (local atomics); after a local grid barrier
+    // CTA i pushes its slice of them into every peer's receive slots
+    // t{ro,rd}[peer][parity][this rank][dim] as tagged 64-bit words, polls its own
+    // slots for every peer's slice, adds the ranks' slices in rank order into X, and
+    // a local grid barrier follows.
+    uint64_t *tro[kMaxTp], *trd[kMaxTp];
+    float *tpo, *tpd;
+    uint32_t *xepoch;                          // exchanges of each kind done so far (kept across launches)
 };
 
 }  // namespace ptc

@@ -38,7 +38,7 @@ constexpr uint32_t kMaxCtas = 256;  // argmax candidates per rank (persistent ke
 // persistent kernel keeps its residual X, FFN delta Y, argmax candidates and
 // barrier flags here so that every rank can add into / write them with peer stores.
 struct Layout {
-    size_t slots, flags, argv, argi, aflags, px, py, pcv, pci, pflag, total;
+    size_t slots, flags, argv, argi, aflags, px, py, pcv, pci, pflag, pro, prd, ppo, ppd, total;
 };
 
 __host__ __device__ inline Layout layout(uint32_t dim) {
@@ -53,7 +53,14 @@ __host__ __device__ inline Layout layout(uint32_t dim) {
     L.pcv = L.py + (size_t)dim * 4;
     L.pci = L.pcv + (size_t)kMaxRanks * kMaxCtas * 4;
     L.pflag = L.pci + (size_t)kMaxRanks * kMaxCtas * 4;  // one 128-byte line per source rank
-    L.total = (L.pflag + (size_t)kMaxRanks * 128 + 255) / 256 * 256;
+    // tensor-core kernel's row-parallel exchange: receive slots [2 parities][source
+    // rank][dim] of tagged 64-bit words for the O and down partials, and this rank's
+    // own partial accumulators
+    L.pro = (L.pflag + (size_t)kMaxRanks * 128 + 255) / 256 * 256;
+    L.prd = L.pro + (size_t)2 * kMaxRanks * dim * 8;
+    L.ppo = L.prd + (size_t)2 * kMaxRanks * dim * 8;
+    L.ppd = L.ppo + (size_t)dim * 4;
+    L.total = (L.ppd + (size_t)dim * 4 + 255) / 256 * 256;
     return L;
 }
 
@@ -449,8 +456,13 @@ void ptc_buffers(const Exchange *x, ptc::TpIn &t) {
         t.cvr[r] = reinterpret_cast<float *>(base + L.pcv);
         t.cir[r] = reinterpret_cast<uint32_t *>(base + L.pci);
         t.flagr[r] = reinterpret_cast<uint32_t *>(base + L.pflag);
+        t.ro[r] = reinterpret_cast<uint64_t *>(base + L.pro);
+        t.rd[r] = reinterpret_cast<uint64_t *>(base + L.prd);
     }
+    t.po = reinterpret_cast<float *>(x->local + L.ppo);
+    t.pd = reinterpret_cast<float *>(x->local + L.ppd);
     t.epoch = x->count + 1;
+    t.xepoch = x->count + 2;
 }
 
 static int launch_cfg(cudaStream_t st, bool pdl, cudaLaunchConfig_t &cfg, cudaLaunchAttribute *attr) {
