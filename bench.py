@@ -131,9 +131,18 @@ class ClockSampler:
         return out
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per token from one ncu capture of the
-# timed launch (profiles/decode_tc_kernel_tinyllama_bs1.md); None where not captured.
-TRAFFIC_PER_TOKEN = {"tensor": (11.329927e9 + 10.755072e6) / 20}
+def traffic_per_token():
+    """dram__bytes_read.sum + dram__bytes_write.sum per token of the decode kernel, from
+    the ncu capture recorded in profiles/dram_traffic.json (keyed by decode path; the
+    file also holds the capture command).  Paths without a capture map to None."""
+    try:
+        rec = json.loads((REPO / "profiles" / "dram_traffic.json").read_text())
+    except Exception:
+        return {}
+    out = {}
+    for path, r in rec.get("decode", {}).items():
+        out[path] = (r["dram_bytes_read"] + r["dram_bytes_write"]) / r["tokens"]
+    return out
 
 DTYPES = {
     "tensor": "e2m1xe8m0 weights x 8-term e2m1xe8m0 activation on tcgen05 kind::mxf4 (exact products, "
@@ -833,8 +842,9 @@ def main():
                    "l2": "no flush: 549.5 MB of weights per step > 126 MB L2"},
         "roofline": {"bound": "hbm", "kernel": f"decode token ({model_path} path)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": TRAFFIC_PER_TOKEN.get(model_path), "bytes_per_launch": wbytes,
-                     "peak_kind": peak_kind, "traffic_source": "ncu dram bytes of a 20-token launch / 20"},
+                     "traffic": traffic_per_token().get(model_path), "bytes_per_launch": wbytes,
+                     "peak_kind": peak_kind,
+                     "traffic_source": "profiles/dram_traffic.json: ncu dram bytes of one launch / its tokens"},
         "gemv": gemv,
         "tp": tpres,
         "cpu_baseline": cpu,
