@@ -333,7 +333,7 @@ size_t mma_ws_need(const fp4x_llama_model *m, uint32_t rows, uint32_t terms) {
 }
 
 // Token-tile rows of the GEMM fed by R rows of terms (the plan's tile width).
-inline uint32_t act_tile_rows(uint32_t m) { return m >= 256 ? 256 : (m + 7) / 8 * 8; }
+inline uint32_t act_tile_rows(uint32_t m) { return mma::token_tile(m); }
 
 template <int SRC>
 int decompose(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, uint32_t K, const float *src, float *x_out,

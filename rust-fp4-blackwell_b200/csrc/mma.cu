@@ -606,6 +606,13 @@ __global__ void __launch_bounds__(128, 1) allones_kernel(float *out) {
     }
 }
 
+// Token rows per CTA tile for an m-row A operand.  128 (not 256): two CTAs share
+// each SM, so one CTA's epilogue and K-stage waits overlap the other's MMA issue,
+// and the grid's last partial wave is half as long (config 3 at M = 512: 824 ->
+// 963 TFLOP/s aggregate).  Callers that pre-arrange activation scale images use the
+// same tiling.
+__host__ __device__ inline uint32_t token_tile(uint32_t m) { return m >= 128 ? 128u : (m + 7) / 8 * 8; }
+
 struct Plan {
     uint32_t nt, m_tiles, n_tiles, kst, kps, splits;
     Geo g;
@@ -613,7 +620,7 @@ struct Plan {
 
 inline Plan plan(uint32_t m, uint32_t n, uint32_t k, bool allow_split = true, bool nv = false) {
     Plan p;
-    p.nt = m >= 256 ? 256 : (m + 7) / 8 * 8;
+    p.nt = token_tile(m);
     p.m_tiles = (m + p.nt - 1) / p.nt;
     p.n_tiles = (n + 127) / 128;
     p.kst = (k + kStageK - 1) / kStageK;

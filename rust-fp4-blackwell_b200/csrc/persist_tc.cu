@@ -42,7 +42,9 @@ constexpr uint32_t kBarLimit = 1u << 24;
 // compiled with -DFP4X_PHASE_TIMING; a no-op otherwise.  kTsPerLayer slots per
 // layer (and the lm_head) per token: consumer steps 0..18, MMA lane 19..23,
 // operand build split (decomposition done / fence done) 24..31, split-attention
-// unit steps 32..34 (q staged, warp 0's positions done, warps merged).
+// unit steps 32..34 (q staged, warp 0's positions done, warps merged), RMSNorm
+// inputs loaded 35, normaliser known 36, K/V appended 37 (the last norm of a
+// layer overwrites 35/36).
 constexpr uint32_t kTsPerLayer = 40;
 #ifdef FP4X_PHASE_TIMING
 constexpr uint32_t kTcStamps = 1u << 15;
@@ -574,9 +576,11 @@ __device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, boo
             for (int j = 0; j < 4; ++j) ss += x[r][j] * x[r][j];
         }
     }
+    CST(35);
     ss = warp_sum(ss);
     if (lane == 0) c.red[warp] = ss;
     csync();
+    CST(36);
     float tot = 0.0f;
 #pragma unroll
     for (int i = 0; i < kCW; ++i) tot += c.red[i];
@@ -664,6 +668,7 @@ __device__ void stage_qkv(Ctx &c, uint32_t l, uint32_t pos) {
         vc[g * HD + j] = f32_to_bf16_bits(__ldcg(vr + j));
         vc[g * HD + j + half] = f32_to_bf16_bits(__ldcg(vr + j + half));
     }
+    CST(37);
     float *qs = reinterpret_cast<float *>(c.smem + c.L.qs);
     const float scale = 1.0f / sqrtf((float)HD);
     for (uint32_t i = threadIdx.x; i < S.nh * half; i += kCons) {
