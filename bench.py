@@ -537,7 +537,8 @@ def tp_section(args, rank, world, torch, dist):
     the same steps in the same order; rank 0 returns the summary."""
     from fp4x import engine, tp
     import numpy as np
-    group = dist.new_group(backend="gloo") if dist else None
+    import datetime
+    group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300)) if dist else None
     st = torch.cuda.current_stream()
     out = {"tp": world, "model": "llama3-8b shape, MXFP4, random init", "context": args.tp_ctx}
 
@@ -823,7 +824,10 @@ def main():
 
     tpres = None
     if not args.no_tp:
-        tpres = tp_section(args, rank, world, torch, dist)
+        try:
+            tpres = tp_section(args, rank, world, torch, dist)
+        except Exception as e:  # the config-1 line above is still reported
+            tpres = {"tp": world, "error": f"{type(e).__name__}: {e}"[:300]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
