@@ -760,12 +760,14 @@ __device__ void attend(Ctx &c, uint32_t l, uint32_t pos) {
     }
     csync();
     float *xv = reinterpret_cast<float *>(c.smem + c.L.xv);
+    // warps past the last position of the sequence hold nothing (m = -inf)
+    const uint32_t act = min(wpg, (seq + 31) / 32);
     for (uint32_t i = tid; i < nh * HD; i += kCons) {
         const uint32_t gh = i / HD, d = i % HD, w0 = gh * wpg;
         float M = -INFINITY;
-        for (uint32_t w = w0; w < w0 + wpg; ++w) M = fmaxf(M, wst[w * (HD + 2)]);
+        for (uint32_t w = w0; w < w0 + act; ++w) M = fmaxf(M, wst[w * (HD + 2)]);
         float L = 0.0f, O = 0.0f;
-        for (uint32_t w = w0; w < w0 + wpg; ++w) {
+        for (uint32_t w = w0; w < w0 + act; ++w) {
             const float mw = wst[w * (HD + 2)];
             const float f = (mw == -INFINITY) ? 0.0f : __expf(mw - M);
             L += wst[w * (HD + 2) + 1] * f;
@@ -942,42 +944,42 @@ __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
         __syncwarp();
     }
     CST(33);
-    // merge the warps per head (fixed order), one head at a time through wst
+    // merge the warps per head (fixed order) through wst.  Only the warps that saw
+    // positions take part (the others hold m = -inf and would add exact zeros); when
+    // their slots for every head fit wst at once, one pass merges all heads.
     float *wst = reinterpret_cast<float *>(c.smem + c.L.wst);  // [kCW][HD + 2]
+    const uint32_t act = max(1u, min((uint32_t)kCW, (t_end - t_begin + 31) / 32));
+    const uint32_t hpp = act * GRP <= (uint32_t)kCW ? (uint32_t)GRP : 1u;  // heads per pass
 #pragma unroll 1
-    for (int h = 0; h < GRP; ++h) {
-        float *ws = wst + warp * (HD + 2);
-        float mh = m[0], lh = lsum[0];
-        float oh[NV];
+    for (int hb = 0; hb < GRP; hb += (int)hpp) {
+        if ((uint32_t)warp < act) {
 #pragma unroll
-        for (int i = 0; i < NV; ++i) oh[i] = o[0][i];
+            for (int h = 0; h < GRP; ++h) {
+                if (h < hb || h >= hb + (int)hpp) continue;
+                float *ws = wst + ((h - hb) * act + warp) * (HD + 2);
+                if (lane == 0) ws[0] = m[h], ws[1] = lsum[h];
 #pragma unroll
-        for (int q = 1; q < GRP; ++q)
-            if (q == h) {
-                mh = m[q], lh = lsum[q];
-#pragma unroll
-                for (int i = 0; i < NV; ++i) oh[i] = o[q][i];
+                for (int cc = 0; cc < HD / 64; ++cc) {
+                    ws[2 + 64 * cc + 2 * lane] = o[h][2 * cc];
+                    ws[2 + 64 * cc + 2 * lane + 1] = o[h][2 * cc + 1];
+                }
             }
-        if (lane == 0) ws[0] = mh, ws[1] = lh;
-#pragma unroll
-        for (int cc = 0; cc < HD / 64; ++cc) {
-            ws[2 + 64 * cc + 2 * lane] = oh[2 * cc];
-            ws[2 + 64 * cc + 2 * lane + 1] = oh[2 * cc + 1];
         }
         csync();
-        float *rec = p.attn_part + ((size_t)(h0 + h) * slices + sl) * (HD + 2);
-        for (uint32_t d = tid; d < HD + 2; d += kCons) {
+        for (uint32_t i = tid; i < hpp * (HD + 2); i += kCons) {
+            const uint32_t hh = i / (HD + 2), d = i % (HD + 2);
+            const float *wh = wst + hh * act * (HD + 2);
             float M = -INFINITY;
-            for (int w = 0; w < kCW; ++w) M = fmaxf(M, wst[w * (HD + 2)]);
+            for (uint32_t w = 0; w < act; ++w) M = fmaxf(M, wh[w * (HD + 2)]);
             float v = M;
             if (d > 0) {
                 v = 0.0f;
-                for (int w = 0; w < kCW; ++w) {
-                    const float mw = wst[w * (HD + 2)];
-                    v += (mw == -INFINITY) ? 0.0f : wst[w * (HD + 2) + d] * __expf(mw - M);
+                for (uint32_t w = 0; w < act; ++w) {
+                    const float mw = wh[w * (HD + 2)];
+                    v += (mw == -INFINITY) ? 0.0f : wh[w * (HD + 2) + d] * __expf(mw - M);
                 }
             }
-            rec[d] = v;
+            p.attn_part[((size_t)(h0 + hb + hh) * slices + sl) * (HD + 2) + d] = v;
         }
         csync();
     }
