@@ -557,6 +557,23 @@ uint32_t choose_splits(uint32_t batch, uint32_t groups, uint32_t seq, uint32_t h
     return pick;
 }
 
+// The combine kernel with programmatic dependent launch: its CTAs may be scheduled
+// while the split kernel runs and wait (griddepcontrol.wait) for its partials, so
+// the second launch's latency overlaps the first kernel.
+template <int HD, typename OT>
+cudaError_t launch_combine(cudaStream_t stream, const Params &p) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_heads, p.batch, HD / kCombineDims);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD, OT>, p);
+}
+
 template <typename QT, typename KT, typename OT>
 int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t seq,
         uint32_t max_seq, const QT *q, const KT *kc, const KT *vc, OT *out, void *ws, size_t ws_bytes,
@@ -586,13 +603,11 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
         if (hd == 64 && hpc == 4) e = launch_mma<64, 4, QT, OT>(stream, p, grid, false);
         if (hd == 128 && hpc == 8) e = launch_mma<128, 8, QT, OT>(stream, p, grid, false);
         if (hd == 128 && hpc == 4) e = launch_mma<128, 4, QT, OT>(stream, p, grid, false);
+        if (e == cudaSuccess && p.splits > 1)
+            e = hd == 64 ? launch_combine<64, OT>(stream, p) : launch_combine<128, OT>(stream, p);
         if (e != cudaSuccess) {
             set_error("llama_attn_decode: %s", cudaGetErrorString(e));
             return FP4X_ECUDA;
-        }
-        if (p.splits > 1) {
-            if (hd == 64) attn_combine_kernel<64, OT><<<dim3(n_heads, batch, 64 / kCombineDims), kCombineThreads, 0, stream>>>(p);
-            else attn_combine_kernel<128, OT><<<dim3(n_heads, batch, 128 / kCombineDims), kCombineThreads, 0, stream>>>(p);
         }
         return check_launch("llama_attn_decode");
     }
