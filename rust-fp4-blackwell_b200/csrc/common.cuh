@@ -176,11 +176,17 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
 }
 
 // Eight codes of one 32-bit word -> four f16x2 (pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7)).
+// The word is split into its four bytes by one vector move (no per-byte
+// extraction and narrowing), then one conversion per byte.
 __device__ __forceinline__ void decode_word_f16(uint32_t w, uint32_t (&h)[4]) {
-    h[0] = e2m1x2_to_f16x2(w & 0xFFu);
-    h[1] = e2m1x2_to_f16x2((w >> 8) & 0xFFu);
-    h[2] = e2m1x2_to_f16x2((w >> 16) & 0xFFu);
-    h[3] = e2m1x2_to_f16x2(w >> 24);
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+        : "r"(w));
 }
 
 // Scalar E2M1 decode in f32, exact; restates llama_run/src/main.rs:21-32 with

@@ -16,7 +16,7 @@
 //     conversion (cvt.rn.f16x2.e2m1x2) and contracted on the tensor cores with
 //     mma.m16n8k16 (column 0 = hi, column 1 = lo), fp32 accumulation; each 32-
 //     block's sum is scaled by its E8M0 scale in fp32;
-//   * the four warps split K and are reduced in a fixed order (deterministic);
+//   * the eight warps split K and are reduced in a fixed order (deterministic);
 //   * prologues fuse RMSNorm (llama_run:79-116) and the embedding gather
 //     (llama_run:509-510); epilogues fuse the residual add (:254-261), SwiGLU
 //     (:244-252) and RoPE + bf16 KV append (:118-146).
