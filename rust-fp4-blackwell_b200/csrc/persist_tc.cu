@@ -455,14 +455,13 @@ __device__ void decompose_lanes(const float *v, uint32_t K, uint8_t *B, uint8_t 
             const int e = term_exp(e1, t);
             const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
             const float s = __uint_as_float((uint32_t)(127 + e) << 23);
-            uint32_t code;
-            asm("{\n\t.reg .b8 q0, q1;\n\t"
-                "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
-                "cvt.rn.satfinite.e2m1x2.f32 q1, %2, %2;\n\t"
-                "mov.b32 %0, {q0, q1, q1, q1};\n\t}"
-                : "=r"(code)
+            uint32_t code, hv;  // the code (low nibble; upper nibble 0) and its value as f16x2
+            asm("{\n\t.reg .b8 q0;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 q0, %3, %2;\n\t"
+                "cvt.u32.u8 %0, q0;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, q0;\n\t}"
+                : "=r"(code), "=r"(hv)
                 : "f"(x * inv), "f"(0.0f));
-            const uint32_t hv = e2m1x2_to_f16x2(code & 0xFFu);
             const __half2 q = *reinterpret_cast<const __half2 *>(&hv);
             x = fmaf(-__low2float(q), s, x);
             uint32_t part = (code & 0xFu) << (4 * (lane & 7));
@@ -502,17 +501,21 @@ __device__ __forceinline__ void decompose_half8(float (&x)[4], uint32_t b, uint3
         const int e = term_exp(e1, t);
         const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
         const float s = __uint_as_float((uint32_t)(127 + e) << 23);
-        uint32_t h;  // 4 nibbles in the low 16 bits
-        asm("{\n\t.reg .b8 q0, q1, z;\n\t"
-            "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
-            "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
-            "cvt.rn.satfinite.e2m1x2.f32 z, %5, %5;\n\t"
-            "mov.b32 %0, {q0, q1, z, z};\n\t}"
-            : "=r"(h)
-            : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv), "f"(0.0f));
+        // the 4 codes (low 16 bits of h) and their values as two f16x2, from the
+        // byte registers the encode leaves (no re-extraction of the bytes)
+        uint32_t h, hvs[2];
+        asm("{\n\t.reg .b8 q0, q1;\n\t.reg .b16 c;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 q0, %4, %3;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 q1, %6, %5;\n\t"
+            "mov.b16 c, {q0, q1};\n\t"
+            "cvt.u32.u16 %0, c;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %1, q0;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %2, q1;\n\t}"
+            : "=r"(h), "=r"(hvs[0]), "=r"(hvs[1])
+            : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv));
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-            const uint32_t hv = e2m1x2_to_f16x2((h >> (8 * q)) & 0xFFu);
+            const uint32_t hv = hvs[q];
             const __half2 d = *reinterpret_cast<const __half2 *>(&hv);
             x[2 * q] = fmaf(-__low2float(d), s, x[2 * q]);
             x[2 * q + 1] = fmaf(-__high2float(d), s, x[2 * q + 1]);
