@@ -511,6 +511,88 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(Params p)
     }
 }
 
+// grid = ceil(batch * n_heads / 8), block = 256: one warp per (b, head) merges all
+// of that head's slices over all HD dims (lane k owns dims [k HD/32, (k+1) HD/32)).
+// This is the form for many (b, head) rows with few slices each (batched decode):
+// the dims-parallel kernel above launches HD/16 CTAs per row there, and at batch 64
+// x 32 heads those 16k short CTAs cost ~50 us of launch waves for ~1 MB of records.
+// Same arithmetic as above (common max, exp weights, sums over slices); the slices
+// are summed in index order.
+template <int HD, typename OT>
+__global__ void __launch_bounds__(256) attn_combine_rows_kernel(Params p) {
+    constexpr int VD = HD / 32, U = 8;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t bh = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (bh >= p.batch * p.n_heads) return;
+    const float *rec = p.ws + (size_t)bh * p.splits * (HD + 2);
+    const uint32_t seq = seq_of(p, bh / p.n_heads);
+    const uint32_t used = (seq + p.split_len - 1) / p.split_len;
+    float m = -INFINITY;
+    for (uint32_t s = lane; s < used; s += 32) m = fmaxf(m, rec[(size_t)s * (HD + 2)]);
+    m = warp_max(m);
+    float l = 0.0f, o[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) o[i] = 0.0f;
+    for (uint32_t base = 0; base < used; base += 32) {
+        const uint32_t cnt = min(32u, used - base);
+        float f = 0.0f;
+        if (lane < cnt) {
+            const float *rs = rec + (size_t)(base + lane) * (HD + 2);
+            f = __expf(rs[0] - m);
+            l += rs[1] * f;
+        }
+        // records are (HD + 2) floats, HD + 2 even: every output pair is 8-byte aligned
+        const float *r = rec + (size_t)base * (HD + 2) + 2 + VD * lane;
+        for (uint32_t j = 0; j < cnt; j += U) {
+            float2 v[U][VD / 2];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int i = 0; i < VD / 2; ++i)
+                    v[u][i] = j + u < cnt ? *reinterpret_cast<const float2 *>(r + (size_t)(j + u) * (HD + 2) + 2 * i)
+                                          : make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float fj = __shfl_sync(0xffffffffu, f, (j + u) & 31);
+                if (j + u < cnt)
+#pragma unroll
+                    for (int i = 0; i < VD / 2; ++i) o[2 * i] += v[u][i].x * fj, o[2 * i + 1] += v[u][i].y * fj;
+            }
+        }
+    }
+    const float L = warp_sum(l);
+    OT *out = reinterpret_cast<OT *>(p.out) + (size_t)bh * HD + VD * lane;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) store_out(out + i, o[i] / L);
+}
+
+// The slice merge for p: the dims-parallel kernel while its HD/16 CTAs per (b, head)
+// fit about two waves of the GPU, else the warp-per-row kernel (at most 256 slices
+// a row; more go to the dims-parallel form, whose chunks keep every load in flight).
+// With pdl, the launch may be scheduled while the split kernel runs.
+template <int HD, typename OT>
+cudaError_t launch_combine(cudaStream_t stream, const Params &p, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const size_t rows = (size_t)p.batch * p.n_heads;
+    const size_t wave = (size_t)num_sms() * (2048 / kCombineThreads);
+    if (rows * (HD / kCombineDims) > 2 * wave && p.splits <= 256) {
+        cfg.gridDim = dim3((unsigned)((rows + 7) / 8));
+        cfg.blockDim = dim3(256);
+        return cudaLaunchKernelEx(&cfg, attn_combine_rows_kernel<HD, OT>, p);
+    }
+    cfg.gridDim = dim3(p.n_heads, p.batch, HD / kCombineDims);
+    cfg.blockDim = dim3(kCombineThreads);
+    return cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD, OT>, p);
+}
+
 // q heads per CTA: the whole GQA group when it is 4 or 8 (else 8 or 4 of it, else 1).
 uint32_t heads_per_cta(uint32_t group, bool group_heads) {
     if (!group_heads) return 1;
@@ -557,23 +639,6 @@ uint32_t choose_splits(uint32_t batch, uint32_t groups, uint32_t seq, uint32_t h
     return pick;
 }
 
-// The combine kernel with programmatic dependent launch: its CTAs may be scheduled
-// while the split kernel runs and wait (griddepcontrol.wait) for its partials, so
-// the second launch's latency overlaps the first kernel.
-template <int HD, typename OT>
-cudaError_t launch_combine(cudaStream_t stream, const Params &p) {
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.n_heads, p.batch, HD / kCombineDims);
-    cfg.blockDim = dim3(kCombineThreads);
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD, OT>, p);
-}
-
 template <typename QT, typename KT, typename OT>
 int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t seq,
         uint32_t max_seq, const QT *q, const KT *kc, const KT *vc, OT *out, void *ws, size_t ws_bytes,
@@ -604,7 +669,7 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
         if (hd == 128 && hpc == 8) e = launch_mma<128, 8, QT, OT>(stream, p, grid, false);
         if (hd == 128 && hpc == 4) e = launch_mma<128, 4, QT, OT>(stream, p, grid, false);
         if (e == cudaSuccess && p.splits > 1)
-            e = hd == 64 ? launch_combine<64, OT>(stream, p) : launch_combine<128, OT>(stream, p);
+            e = hd == 64 ? launch_combine<64, OT>(stream, p, true) : launch_combine<128, OT>(stream, p, true);
         if (e != cudaSuccess) {
             set_error("llama_attn_decode: %s", cudaGetErrorString(e));
             return FP4X_ECUDA;
@@ -614,7 +679,7 @@ int run(cudaStream_t stream, uint32_t batch, uint32_t n_heads, uint32_t n_kv, ui
 #define FP4X_ATTN_CASE(HD_, HPC_)                                                                       \
     if (hd == HD_ && hpc == HPC_) {                                                                   \
         attn_split_kernel<HD_, HPC_, QT, KT, OT><<<grid, kThreads, 0, stream>>>(p);                   \
-        if (p.splits > 1) attn_combine_kernel<HD_, OT><<<dim3(n_heads, batch, HD_ / kCombineDims), kCombineThreads, 0, stream>>>(p); \
+        if (p.splits > 1) (void)launch_combine<HD_, OT>(stream, p, false);                           \
     }
     FP4X_ATTN_CASE(64, 1)
     FP4X_ATTN_CASE(64, 4)
@@ -642,12 +707,7 @@ int launch_engine_t(cudaStream_t stream, const Params &p, bool pdl) {
     cfg.numAttrs = pdl ? 1 : 0;
     cudaError_t e = (HPC == 4 || HPC == 8) ? launch_mma<HD, HPC, float, float>(stream, p, cfg.gridDim, pdl)
                                             : cudaLaunchKernelEx(&cfg, attn_split_kernel<HD, HPC, float, uint16_t, float>, p);
-    if (e == cudaSuccess && p.splits > 1) {
-        cudaLaunchConfig_t c2 = cfg;
-        c2.gridDim = dim3(p.n_heads, p.batch, HD / kCombineDims);
-        c2.blockDim = dim3(kCombineThreads);
-        e = cudaLaunchKernelEx(&c2, attn_combine_kernel<HD, float>, p);
-    }
+    if (e == cudaSuccess && p.splits > 1) e = launch_combine<HD, float>(stream, p, pdl);
     if (e != cudaSuccess) {
         set_error("attention (engine): %s", cudaGetErrorString(e));
         return FP4X_ECUDA;
