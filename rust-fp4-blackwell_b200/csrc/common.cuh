@@ -125,6 +125,9 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 __device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void prefetch_l2_line(const void *src) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(src) : "memory");
+}
 
 // ---------------------------------------------------------------- PDL
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -44,7 +44,8 @@ constexpr uint32_t kBarLimit = 1u << 24;
 // operand build split (decomposition done / fence done) 24..31, split-attention
 // unit steps 32..34 (q staged, warp 0's positions done, warps merged), RMSNorm
 // inputs loaded 35, normaliser known 36, K/V appended 37 (the last norm of a
-// layer overwrites 35/36).
+// layer overwrites 35/36), split-attention warp 0's scores done 38 and softmax
+// done 39 (its last tile).
 constexpr uint32_t kTsPerLayer = 40;
 #ifdef FP4X_PHASE_TIMING
 constexpr uint32_t kTcStamps = 1u << 15;
@@ -103,7 +104,7 @@ __host__ __device__ inline Smem smem_layout(const Params &p) {
     L.sfbo = take((attn_k(p) / 128 + 1 + 3) * 128, 128);
     L.bh = take(5 * 128, 128);                       // U <= 128: 4 k32 columns, then a zero column
     L.sfbh = take((2 + 3) * 128, 128);
-    L.qs = take(kMaxGroup * p.hd * 4, 16);
+    L.qs = take(kMaxGroup * (p.hd + p.hd / 8) * 4, 16);  // split attention pads 4 floats per 32 dims
     L.wst = take(kCW * (p.hd + 2) * 4, 16);
     L.gu = take(256 * 4, 16);
     L.ps = take(kCW * kMaxGroup * 32 * 4, 16);  // split attention: per-warp probabilities
@@ -600,10 +601,32 @@ __device__ void norm_decompose(Ctx &c, const uint16_t *erow, const float *w, boo
     }
 }
 
+// Split attention, issued during layer l's QKV phase: L2 prefetch of the K and V
+// rows (positions before pos) that this CTA's attention unit reads after the QKV
+// barrier, so the unit's loads meet L2 instead of HBM.  One bulk prefetch per
+// cached row (a KV head's HD bf16 values; rows of one head are n_kv * HD apart),
+// spread over the consumer threads.
+__device__ void prefetch_unit_kv(Ctx &c, uint32_t l, uint32_t pos) {
+    const Params &p = *c.p;
+    const uint32_t slices = p.attn_slices, u = blockIdx.x;
+    if (u >= p.n_kv * slices) return;
+    const uint32_t g = u / slices, sl = u % slices, seq = pos + 1;
+    const uint32_t len = (seq + slices - 1) / slices, t_begin = min(seq, sl * len), t_end = min(pos, t_begin + len);
+    if (t_begin >= t_end) return;
+    const size_t base = (size_t)l * p.max_seq * p.kvd + (size_t)g * p.hd;
+    const uint32_t n = t_end - t_begin, bytes = p.hd * 2;
+    for (uint32_t i = threadIdx.x; i < 2 * n; i += kCons) {
+        const uint16_t *src = (i < n ? p.kc : p.vc) + base + (size_t)(t_begin + (i < n ? i : i - n)) * p.kvd;
+        prefetch_l2_bulk(src, bytes);
+    }
+}
+
 // ---------------------------------------------------------------- phases
 
 // A: normed input -> 8 terms -> QKV unit MMAs -> partial row sums into p.qkv.
-__device__ void phase_qkv(Ctx &c, uint32_t l, uint32_t tok, uint32_t lay_count) {
+// With kv_pos >= 0 (split attention this layer) the CTA's attention-unit K/V rows
+// are prefetched into L2 while the QKV MMAs run.
+__device__ void phase_qkv(Ctx &c, uint32_t l, uint32_t tok, uint32_t lay_count, int kv_pos) {
     const Params &p = *c.p;
     const Sched &S = *c.S;
     if (l == 0)
@@ -613,8 +636,9 @@ __device__ void phase_qkv(Ctx &c, uint32_t l, uint32_t tok, uint32_t lay_count) 
     else
         norm_decompose<1>(c, nullptr, p.attn_norm + (size_t)l * p.dim, S.n_a > 0);
     CST(1);
+    if (S.n_a > 0) signal_operand(c, PH_QKV);
+    if (kv_pos >= 0) prefetch_unit_kv(c, l, (uint32_t)kv_pos);
     if (S.n_a == 0) return;
-    signal_operand(c, PH_QKV);
     CST(2);
     wait_acc(c, PH_QKV, lay_count & 1);
     CST(3);
@@ -841,30 +865,192 @@ __device__ void phase_attn_o(Ctx &c, uint32_t l, uint32_t pos, uint32_t lay_coun
 
 // Split attention for long contexts, part 1: unit u = (KV head g, slice s) of the
 // sequence (one unit per CTA, units = n_kv * attn_slices), all q heads of the GQA
-// group at once (each K/V row read once per unit).  Lane = token for Q.K, lane =
-// head-dim pair for P.V (probabilities through shared memory).  The unit holding
-// the current position also RoPEs and appends its K/V (bf16).  Writes per head the
-// slice's (max, sum, unnormalised output) to attn_part[head][slice].
+// group at once (each K/V row read once per unit).  The unit holding the current
+// position also RoPEs and appends its K/V (bf16).  Writes per head the slice's
+// (max, sum, unnormalised output) to attn_part[head][slice].
+//
+// Every consumer warp takes RW consecutive rows of a pass of kCW * RW positions
+// (RW the smallest of 2, 4, 8 that covers the unit in one pass, else 8 and more
+// passes, so a short slice still spreads over all warps): a row's Q.K is split
+// over 32 / RW lanes (HD * RW / 32 dims each, vector loads of K and of the padded
+// q) and summed with xor shuffles; the warp's V rows are loaded with its K rows;
+// the softmax uses the CTA-wide maximum of each head (one exchange per pass), so
+// the warps' outputs and sums merge by plain addition, done as a fixed-order tree
+// in shared memory; P.V has lane = head-dim pair.
+template <int HD, int GRP, int RW>
+__device__ void unit_scan(Ctx &c, const float *qs, const uint16_t *kb, const uint16_t *vb, size_t row,
+                          uint32_t t_begin, uint32_t t_end, float *rec0, uint32_t rec_stride) {
+    constexpr int LPR = 32 / RW, DPL = HD / LPR, NV = HD / 32, QP = HD + HD / 8;
+    static_assert(DPL % 4 == 0, "unit_scan: at least 4 dims per lane");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t r_in = lane / LPR, seg = lane % LPR;
+    float *ps = reinterpret_cast<float *>(c.smem + c.L.ps) + warp * (kMaxGroup * 32);
+    float *wmax = c.red, *wsum = c.red + kCW * kMaxGroup;  // [kCW][GRP] each
+    float M[GRP], lsum[GRP], o[GRP][NV];
+#pragma unroll
+    for (int h = 0; h < GRP; ++h) {
+        M[h] = -INFINITY, lsum[h] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) o[h][i] = 0.0f;
+    }
+    for (uint32_t base = t_begin; base < t_end; base += kCW * RW) {  // uniform over the CTA
+        const uint32_t t0 = base + warp * RW, t = t0 + r_in;
+        const bool live = t < t_end;
+        const uint32_t nt = t0 < t_end ? min((uint32_t)RW, t_end - t0) : 0u;
+        // this warp's V rows (lane = head-dim pair), loaded before the scores exist
+        uint32_t vw[RW][HD / 64];
+#pragma unroll
+        for (int j = 0; j < RW; ++j)
+#pragma unroll
+            for (int cc = 0; cc < HD / 64; ++cc)
+                vw[j][cc] = (uint32_t)j < nt ? __ldcg(reinterpret_cast<const uint32_t *>(vb + (size_t)(t0 + j) * row) + 32 * cc + lane) : 0u;
+        float sc[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) sc[h] = 0.0f;
+        if (live) {
+            const uint32_t d0 = seg * DPL;
+            const uint16_t *kr = kb + (size_t)t * row + d0;
+#pragma unroll
+            for (int cc = 0; cc < (DPL + 7) / 8; ++cc) {
+                float kv[8];
+                if (DPL >= 8) {
+                    const uint4 kq = __ldcg(reinterpret_cast<const uint4 *>(kr) + cc);
+                    const uint32_t wv[4] = {kq.x, kq.y, kq.z, kq.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        kv[2 * j] = __uint_as_float(wv[j] << 16), kv[2 * j + 1] = __uint_as_float(wv[j] & 0xFFFF0000u);
+                } else {
+                    const uint2 kq = __ldcg(reinterpret_cast<const uint2 *>(kr));
+                    kv[0] = __uint_as_float(kq.x << 16), kv[1] = __uint_as_float(kq.x & 0xFFFF0000u);
+                    kv[2] = __uint_as_float(kq.y << 16), kv[3] = __uint_as_float(kq.y & 0xFFFF0000u);
+                }
+                const uint32_t d = d0 + 8 * cc, qo = d + (d >> 5) * 4;  // padded q index of dim d
+#pragma unroll
+                for (int h = 0; h < GRP; ++h) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(qs + h * QP + qo);
+                    sc[h] += qa.x * kv[0] + qa.y * kv[1] + qa.z * kv[2] + qa.w * kv[3];
+                    if (DPL >= 8) {
+                        const float4 qb = *reinterpret_cast<const float4 *>(qs + h * QP + qo + 4);
+                        sc[h] += qb.x * kv[4] + qb.y * kv[5] + qb.z * kv[6] + qb.w * kv[7];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+#pragma unroll
+            for (int off = LPR / 2; off > 0; off >>= 1) sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], off);
+            const float wm = warp_max(live ? sc[h] : -INFINITY);
+            if (lane == 0) wmax[warp * GRP + h] = wm;
+        }
+        CST(38);
+        csync();
+        float mn[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            mn[h] = M[h];
+            for (int w = 0; w < kCW; ++w) mn[h] = fmaxf(mn[h], wmax[w * GRP + h]);
+            const float alpha = __expf(M[h] - mn[h]);  // M = -inf on the first pass -> 0
+            const float pr = live ? __expf(sc[h] - mn[h]) : 0.0f;
+            lsum[h] = lsum[h] * alpha + warp_sum(seg == 0 ? pr : 0.0f);
+            if (seg == 0) ps[h * 32 + r_in] = pr;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) o[h][i] *= alpha;
+            M[h] = mn[h];
+        }
+        __syncwarp();
+        CST(39);
+#pragma unroll
+        for (int j = 0; j < RW; ++j) {
+            if ((uint32_t)j >= nt) break;
+            float v[NV];
+#pragma unroll
+            for (int cc = 0; cc < HD / 64; ++cc) {
+                v[2 * cc] = __uint_as_float(vw[j][cc] << 16);
+                v[2 * cc + 1] = __uint_as_float(vw[j][cc] & 0xFFFF0000u);
+            }
+#pragma unroll
+            for (int h = 0; h < GRP; ++h) {
+                const float pr = ps[h * 32 + j];
+#pragma unroll
+                for (int i = 0; i < NV; ++i) o[h][i] += pr * v[i];
+            }
+        }
+        csync();  // wmax and ps are rewritten by the next pass (or the merge)
+    }
+    CST(33);
+    // warps w and w + half merge (w < half), half = 8, 4, 2, 1: outputs through the
+    // probability area (kCW * kMaxGroup * 32 floats), HC heads per tree so that 8
+    // warps x HC x HD values fit it; sums through wsum.  Every warp takes part; warps
+    // without rows add zeros.
+    constexpr int HC = (kCW * kMaxGroup * 32) / (kCW / 2 * HD) < GRP ? (kCW * kMaxGroup * 32) / (kCW / 2 * HD) : GRP;
+    static_assert(HC >= 1 && GRP % HC == 0, "unit_scan: merge chunking");
+    float *mrg = reinterpret_cast<float *>(c.smem + c.L.ps);
+#pragma unroll
+    for (int hb = 0; hb < GRP; hb += HC) {
+#pragma unroll 1
+        for (int half = kCW / 2; half > 0; half >>= 1) {
+            if (warp >= half && warp < 2 * half) {
+                float *dst = mrg + (warp - half) * (HC * HD);
+#pragma unroll
+                for (int h = hb; h < hb + HC; ++h) {
+#pragma unroll
+                    for (int cc = 0; cc < HD / 64; ++cc)
+                        *reinterpret_cast<float2 *>(dst + (h - hb) * HD + 64 * cc + 2 * lane) =
+                            make_float2(o[h][2 * cc], o[h][2 * cc + 1]);
+                    if (lane == 0) wsum[(warp - half) * GRP + h] = lsum[h];
+                }
+            }
+            csync();
+            if (warp < half) {
+                const float *src = mrg + warp * (HC * HD);
+#pragma unroll
+                for (int h = hb; h < hb + HC; ++h) {
+#pragma unroll
+                    for (int cc = 0; cc < HD / 64; ++cc) {
+                        const float2 v = *reinterpret_cast<const float2 *>(src + (h - hb) * HD + 64 * cc + 2 * lane);
+                        o[h][2 * cc] += v.x, o[h][2 * cc + 1] += v.y;
+                    }
+                    lsum[h] += wsum[warp * GRP + h];
+                }
+            }
+            csync();
+        }
+    }
+    if (warp == 0) {
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            float *r = rec0 + (size_t)h * rec_stride;
+            if (lane == 0) r[0] = M[h], r[1] = lsum[h];
+#pragma unroll
+            for (int cc = 0; cc < HD / 64; ++cc)
+                *reinterpret_cast<float2 *>(r + 2 + 64 * cc + 2 * lane) = make_float2(o[h][2 * cc], o[h][2 * cc + 1]);
+        }
+    }
+}
+
 template <int HD, int GRP>
 __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
     const Params &p = *c.p;
-    constexpr int NV = HD / 32;
     constexpr uint32_t half = HD / 2;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+    const int tid = threadIdx.x;
     const uint32_t slices = p.attn_slices, u = blockIdx.x;
     if (u >= p.n_kv * slices) return;
     const uint32_t g = u / slices, sl = u % slices, seq = pos + 1;
     const uint32_t len = (seq + slices - 1) / slices, t_begin = min(seq, sl * len), t_end = min(seq, t_begin + len);
     const uint32_t h0 = g * GRP;
-    float *qs = reinterpret_cast<float *>(c.smem + c.L.qs);  // [GRP][HD]
+    // [GRP][HD + HD / 8]: 4 floats of padding after every 32 dims, so the lanes of a
+    // warp that read different dims of q hit different banks
+    float *qs = reinterpret_cast<float *>(c.smem + c.L.qs);
+    constexpr uint32_t QP = HD + HD / 8;
     const float *cs = p.cos_t + (size_t)pos * half, *sn = p.sin_t + (size_t)pos * half;
     const float scale = 1.0f / sqrtf((float)HD);
     for (uint32_t i = tid; i < GRP * half; i += kCons) {
-        const uint32_t hh = i / half, j = i % half;
+        const uint32_t hh = i / half, j = i % half, j2 = j + half;
         const float *qr = p.qkv + (h0 + hh) * HD;
-        const float q0 = __ldcg(qr + j), q1 = __ldcg(qr + j + half);
-        qs[hh * HD + j] = __fsub_rn(__fmul_rn(q0, cs[j]), __fmul_rn(q1, sn[j])) * scale;
-        qs[hh * HD + j + half] = __fadd_rn(__fmul_rn(q1, cs[j]), __fmul_rn(q0, sn[j])) * scale;
+        const float q0 = __ldcg(qr + j), q1 = __ldcg(qr + j2);
+        qs[hh * QP + j + (j >> 5) * 4] = __fsub_rn(__fmul_rn(q0, cs[j]), __fmul_rn(q1, sn[j])) * scale;
+        qs[hh * QP + j2 + (j2 >> 5) * 4] = __fadd_rn(__fmul_rn(q1, cs[j]), __fmul_rn(q0, sn[j])) * scale;
     }
     const size_t row = p.kvd;
     uint16_t *kb = p.kc + (size_t)l * p.max_seq * row + g * HD, *vb = p.vc + (size_t)l * p.max_seq * row + g * HD;
@@ -879,112 +1065,17 @@ __device__ void attend_unit(Ctx &c, uint32_t l, uint32_t pos) {
     }
     csync();
     CST(32);
-    float *ps = reinterpret_cast<float *>(c.smem + c.L.ps) + warp * (kMaxGroup * 32);
-    float m[GRP], lsum[GRP], o[GRP][NV];
-#pragma unroll
-    for (int h = 0; h < GRP; ++h) {
-        m[h] = -INFINITY, lsum[h] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < NV; ++i) o[h][i] = 0.0f;
-    }
-    for (uint32_t t0 = t_begin + 32 * warp; t0 < t_end; t0 += 32 * kCW) {
-        const uint32_t t = t0 + lane;
-        const bool live = t < t_end;
-        float sc[GRP];
-#pragma unroll
-        for (int h = 0; h < GRP; ++h) sc[h] = 0.0f;
-        if (live) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)t * row);
-#pragma unroll
-            for (int cc = 0; cc < HD / 8; ++cc) {
-                const uint4 kq = __ldcg(kr + cc);
-                const uint32_t wv[4] = {kq.x, kq.y, kq.z, kq.w};
-                float kv[8];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    kv[2 * j] = __uint_as_float(wv[j] << 16);
-                    kv[2 * j + 1] = __uint_as_float(wv[j] & 0xFFFF0000u);
-                }
-#pragma unroll
-                for (int h = 0; h < GRP; ++h) {
-                    const float *q = qs + h * HD + 8 * cc;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) sc[h] += q[j] * kv[j];
-                }
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < GRP; ++h) {
-            const float sh = live ? sc[h] : -INFINITY;
-            const float mn = fmaxf(m[h], warp_max(sh));
-            const float alpha = __expf(m[h] - mn);
-            const float pr = live ? __expf(sh - mn) : 0.0f;
-            lsum[h] = lsum[h] * alpha + warp_sum(pr);
-            m[h] = mn;
-            ps[h * 32 + lane] = pr;
-#pragma unroll
-            for (int i = 0; i < NV; ++i) o[h][i] *= alpha;
-        }
-        __syncwarp();
-        const uint32_t nt = min(32u, t_end - t0);
-#pragma unroll 4
-        for (uint32_t j = 0; j < nt; ++j) {
-            const uint32_t *vr = reinterpret_cast<const uint32_t *>(vb + (size_t)(t0 + j) * row);
-            float v[NV];
-#pragma unroll
-            for (int cc = 0; cc < HD / 64; ++cc) {
-                const uint32_t w = __ldcg(vr + 32 * cc + lane);
-                v[2 * cc] = __uint_as_float(w << 16);
-                v[2 * cc + 1] = __uint_as_float(w & 0xFFFF0000u);
-            }
-#pragma unroll
-            for (int h = 0; h < GRP; ++h) {
-                const float pr = ps[h * 32 + j];
-#pragma unroll
-                for (int i = 0; i < NV; ++i) o[h][i] += pr * v[i];
-            }
-        }
-        __syncwarp();
-    }
-    CST(33);
-    // merge the warps per head (fixed order) through wst.  Only the warps that saw
-    // positions take part (the others hold m = -inf and would add exact zeros); when
-    // their slots for every head fit wst at once, one pass merges all heads.
-    float *wst = reinterpret_cast<float *>(c.smem + c.L.wst);  // [kCW][HD + 2]
-    const uint32_t act = max(1u, min((uint32_t)kCW, (t_end - t_begin + 31) / 32));
-    const uint32_t hpp = act * GRP <= (uint32_t)kCW ? (uint32_t)GRP : 1u;  // heads per pass
+    // heads scanned together: at most 4 of 128 dims (8 would hold 32 more
+    // accumulators per lane than the kernel's register budget leaves)
+    constexpr int GS = HD * GRP > 512 ? 512 / HD : GRP;
+    const uint32_t n = t_end - t_begin, stride = slices * (HD + 2);
 #pragma unroll 1
-    for (int hb = 0; hb < GRP; hb += (int)hpp) {
-        if ((uint32_t)warp < act) {
-#pragma unroll
-            for (int h = 0; h < GRP; ++h) {
-                if (h < hb || h >= hb + (int)hpp) continue;
-                float *ws = wst + ((h - hb) * act + warp) * (HD + 2);
-                if (lane == 0) ws[0] = m[h], ws[1] = lsum[h];
-#pragma unroll
-                for (int cc = 0; cc < HD / 64; ++cc) {
-                    ws[2 + 64 * cc + 2 * lane] = o[h][2 * cc];
-                    ws[2 + 64 * cc + 2 * lane + 1] = o[h][2 * cc + 1];
-                }
-            }
-        }
-        csync();
-        for (uint32_t i = tid; i < hpp * (HD + 2); i += kCons) {
-            const uint32_t hh = i / (HD + 2), d = i % (HD + 2);
-            const float *wh = wst + hh * act * (HD + 2);
-            float M = -INFINITY;
-            for (uint32_t w = 0; w < act; ++w) M = fmaxf(M, wh[w * (HD + 2)]);
-            float v = M;
-            if (d > 0) {
-                v = 0.0f;
-                for (uint32_t w = 0; w < act; ++w) {
-                    const float mw = wh[w * (HD + 2)];
-                    v += (mw == -INFINITY) ? 0.0f : wh[w * (HD + 2) + d] * __expf(mw - M);
-                }
-            }
-            p.attn_part[((size_t)(h0 + hb + hh) * slices + sl) * (HD + 2) + d] = v;
-        }
-        csync();
+    for (int hs = 0; hs < GRP; hs += GS) {
+        float *rec0 = p.attn_part + ((size_t)(h0 + hs) * slices + sl) * (HD + 2);
+        const float *q = qs + hs * QP;
+        if (n <= 2u * kCW) unit_scan<HD, GS, 2>(c, q, kb, vb, row, t_begin, t_end, rec0, stride);
+        else if (n <= 4u * kCW) unit_scan<HD, GS, 4>(c, q, kb, vb, row, t_begin, t_end, rec0, stride);
+        else unit_scan<HD, GS, 8>(c, q, kb, vb, row, t_begin, t_end, rec0, stride);
     }
     CST(34);
 }
@@ -1045,7 +1136,7 @@ __device__ void phase_attn_combine_o(Ctx &c, uint32_t lay_count) {
     for (uint32_t i = tid; i < G * cols; i += kCons) {
         const uint32_t g = i / cols, col = i % cols, hs = col / hd, d = col % hd;
         float O = 0.0f;
-#pragma unroll 4
+#pragma unroll 16
         for (uint32_t s2 = g; s2 < NS; s2 += G) O += fm[hs * NS + s2] * __ldcg(rec(hs, s2) + 2 + d);
         part[i] = O;
     }
@@ -1409,10 +1500,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(Params p) {
                 const uint32_t lc = it * p.n_layers + l;
                 c.tsb = (it * (p.n_layers + 1) + l) * kTsPerLayer;
                 CST(0);
-                phase_qkv(c, l, tok, lc);
+                const bool split = p.attn_slices && pos + 1 > kSplitMinSeq;  // same decision in every CTA
+                phase_qkv(c, l, tok, lc, split ? (int)pos : -1);
                 if (!grid_barrier(c)) break;
                 CST(5);
-                if (p.attn_slices && pos + 1 > kSplitMinSeq) {  // same decision in every CTA
+                if (split) {
                     phase_attn_units(c, l, pos);
                     if (!grid_barrier(c)) break;
                     phase_attn_combine_o(c, lc);

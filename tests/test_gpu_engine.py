@@ -187,6 +187,36 @@ def test_engine_long_context_split_attention(cfg):
     print(f"long context: worst logits rel err {worst:.3e}")
 
 
+# Split-attention unit geometries of the 8B shape (8 KV heads of 128 dims, 4 q heads
+# each) and of an 8-heads-per-KV-head group at 128 dims (scanned in two halves).
+# With 148 CTAs a unit covers seq / (148 / n_kv) positions, so the checked positions
+# walk the unit scan through 2, 4 and 8 rows per warp and then two passes.
+SPLIT_G4 = dict(n_layers=2, dim=512, ffn=512, n_heads=32, n_kv_heads=8, head_dim=128, vocab=500, max_seq=2400,
+                rope_theta=500000.0, eps=1e-5, seed=7)
+SPLIT_G8 = dict(SPLIT_G4, n_heads=16, n_kv_heads=2, seed=8)
+
+
+@pytest.mark.parametrize("cfg,checks", [(SPLIT_G4, (520, 700, 1300, 2300, 2399)), (SPLIT_G8, (520, 2399))],
+                         ids=["8b-units", "group8-hd128"])
+def test_engine_split_attention_unit_geometries(cfg, checks):
+    """Long-context split attention at the 8B shape's unit geometry: logits within
+    1e-2 of the oracle at positions whose units take 2, 4 and 8 rows per warp and
+    more than one pass (teacher forcing on a seeded token stream)."""
+    toks = oracle.uniform_ids(23, cfg["vocab"], cfg["max_seq"])
+    ref = oracle.Model(cfg)
+    with engine.Model(cfg) as m:
+        assert m.path == "tensor"
+        worst = 0.0
+        for pos, t in enumerate(toks):
+            want = pos in checks
+            gn, gl = m.forward(int(t), pos, want_logits=want)
+            rn, rl = ref.forward(int(t), pos)
+            if want:
+                worst = max(worst, compare_logits(gl, rl))
+    ref.close()
+    print(f"split units: worst logits rel err {worst:.3e}")
+
+
 @pytest.mark.parametrize("path", ["graph", "tensor"])
 def test_generate_batched_prefill_matches_oracle_long_prompt(path, monkeypatch):
     """llama_generate prefills the prompt through the batched engine (passes of 64
