@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(kThreads) rows_decompose_kernel(uint32_t K, co
                                                                   uint8_t *act_s, uint32_t row0, uint32_t terms,
                                                                   uint32_t img_nt) {
     __shared__ float red[kThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t r = blockIdx.x, rs = row0 + r;  // output row, source row
     const uint32_t nw = K / 8, i = blockIdx.y * kThreads + threadIdx.x;
     const uint16_t *erow = SRC == SRC_EMBED ? embed + (size_t)tok[rs] * K : nullptr;
@@ -200,6 +202,8 @@ __global__ void __launch_bounds__(kThreads) rows_rope_append_kernel(uint32_t qd,
                                                                     uint16_t *vc, const uint32_t *pos,
                                                                     const uint32_t *cache, uint32_t max_seq,
                                                                     const float *cos_t, const float *sin_t) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t r = blockIdx.x, half = hd / 2, n = qd + 2 * kvd, pairs = (qd + kvd) / 2;
     const uint32_t p = pos[r];
     const size_t c = cache ? cache[r] : r;
@@ -339,9 +343,13 @@ template <int SRC>
 int decompose(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, uint32_t K, const float *src, float *x_out,
               const uint32_t *tok, const float *norm_w, uint32_t row0 = 0) {
     const uint32_t chunks = (K / 8 + kThreads - 1) / kThreads;
-    rows_decompose_kernel<SRC><<<dim3(R, chunks), kThreads, 0, st>>>(
-        K, src, x_out, b->m->embed, tok, norm_w, b->m->lc.eps, b->act, b->act_s, row0, b->terms,
-        act_tile_rows(R * b->terms));
+    const cudaError_t e = launch_pdl(rows_decompose_kernel<SRC>, dim3(R, chunks), dim3(kThreads), 0, st, K, src, x_out,
+                                     (const uint16_t *)b->m->embed, tok, norm_w, b->m->lc.eps, b->act, b->act_s, row0,
+                                     b->terms, act_tile_rows(R * b->terms));
+    if (e != cudaSuccess) {
+        set_error("llama_batch: decompose: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
+    }
     return check_launch("llama_batch: decompose");
 }
 
@@ -384,11 +392,15 @@ int forward(fp4x_llama_batch *b, cudaStream_t st, uint32_t R, const uint32_t *to
             FP4X_TRY(decompose<SRC_NORM>(b, st, R, c.dim, b->x, nullptr, nullptr, L.attn_norm));
         const uint8_t *const *wi = b->wimg.data() + 4 * l;
         FP4X_TRY(linear(b, st, R, L.qkv, wi[0], b->qkv, false));
-        rows_rope_append_kernel<<<dim3(R, (qd + 3 * kvd + 2 * kThreads - 1) / (2 * kThreads)), kThreads, 0, st>>>(qd, kvd, hd, b->qkv, b->q, kc, vc, pos, cache, b->max_seq,
-                                                        m->cos_t, m->sin_t);
+        if (launch_pdl(rows_rope_append_kernel, dim3(R, (qd + 3 * kvd + 2 * kThreads - 1) / (2 * kThreads)),
+                       dim3(kThreads), 0, st, qd, kvd, hd, b->qkv, b->q, kc, vc, pos, cache, b->max_seq,
+                       (const float *)m->cos_t, (const float *)m->sin_t) != cudaSuccess) {
+            set_error("llama_batch: rope launch failed");
+            return FP4X_ECUDA;
+        }
         FP4X_TRY(check_launch("llama_batch: rope"));
         ap.kc = kc, ap.vc = vc;
-        FP4X_TRY(attn::launch_engine(st, ap, hd, false));
+        FP4X_TRY(attn::launch_engine(st, ap, hd, true));
         FP4X_TRY(decompose<SRC_PLAIN>(b, st, R, qd, b->att, nullptr, nullptr, nullptr));
         if (b->rx) {  // row-parallel O: local partial, then the cross-rank sum into the residual
             FP4X_TRY(linear(b, st, R, L.o, wi[1], b->part, false));

@@ -203,6 +203,8 @@ __device__ __forceinline__ void emit(const Args &a, uint32_t tok, uint32_t row, 
 // Split-K: out[t][r] (final write of `mode`) = sum over splits, in split order.
 __global__ void splitk_reduce_kernel(const float *__restrict__ ws, uint32_t splits, uint32_t tokens, uint32_t n,
                                      void *d, uint32_t mode) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t total = (size_t)tokens * n, stride = (size_t)gridDim.x * blockDim.x;
     Args a{};
     a.n = n, a.d = d, a.mode = mode;
@@ -412,6 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tbase = *tmem_slot;
+    // Launched with programmatic dependent launch: the setup above overlaps the
+    // previous kernel's tail; nothing the previous kernel writes (operands, scales,
+    // the output) is touched before it has completed.
+    pdl_launch_dependents();
+    pdl_wait();
     if (threadIdx.x == 0) mts(1);
 
     if (warp == 0) {
@@ -699,15 +706,32 @@ int launch(cudaStream_t s, uint32_t m, uint32_t n, uint32_t k, const uint8_t *a,
             ok = tc::make_map_out(&map_d, d, mode == OUT_BF16 ? 2 : 4, n, tokens, 1, 128, box_rows);
         args.tma_out = ok ? 1u : 0u;
     }
-    const dim3 grid(p.m_tiles, p.n_tiles, p.splits);
-    if (nv)
-        mxf4_gemm_kernel<true><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, map_d, args);
-    else
-        mxf4_gemm_kernel<false><<<grid, kThreads, p.g.smem, s>>>(map_w, map_a, map_d, args);
-    if (p.splits > 1) {
+    // Both kernels wait (griddepcontrol.wait) before touching memory, so they are
+    // launched with programmatic dependent launch: their launch and setup overlap
+    // the previous kernel on the stream.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.m_tiles, p.n_tiles, p.splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.g.smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = nv ? cudaLaunchKernelEx(&cfg, mxf4_gemm_kernel<true>, map_w, map_a, map_d, args)
+                       : cudaLaunchKernelEx(&cfg, mxf4_gemm_kernel<false>, map_w, map_a, map_d, args);
+    if (e == cudaSuccess && p.splits > 1) {
         const size_t total = (size_t)(m / terms) * n;
-        const uint32_t blocks = (uint32_t)std::min<size_t>((total / 4 + 255) / 256 + 1, 8u * (uint32_t)num_sms());
-        splitk_reduce_kernel<<<blocks, 256, 0, s>>>(partials, p.splits, m / terms, n, d, (uint32_t)mode);
+        cfg.gridDim = dim3((uint32_t)std::min<size_t>((total / 4 + 255) / 256 + 1, 8u * (uint32_t)num_sms()));
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = 0;
+        e = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, (const float *)partials, p.splits, m / terms, n, d,
+                               (uint32_t)mode);
+    }
+    if (e != cudaSuccess) {
+        set_error("fp4_mma: launch: %s", cudaGetErrorString(e));
+        return FP4X_ECUDA;
     }
     return check_launch("fp4_mma");
 }
