@@ -1151,6 +1151,40 @@ __device__ void phase_attn_combine_o(Ctx &c, uint32_t lay_count) {
     o_projection(c, lay_count);
 }
 
+// The two CTAs of a K-split FFN pair meet: each has stored its partial gate/up sums
+// (this layer's) into its half of p.ffx; its flag word (cleared before every launch)
+// is released with the layer's barrier count, and the partner's is awaited
+// (bounded, abort-aware).  Uniform result over the CTA.
+__device__ bool ffn_pair_exchange(Ctx &c, const Sched &S) {
+    const Params &p = *c.p;
+    volatile uint32_t *flag = reinterpret_cast<volatile uint32_t *>(c.smem + c.L.flag);
+    uint32_t *fl = p.bar + 4 + (S.f0 / 64) * 2;
+    const uint32_t tag = c.nbar;  // >= 1 here, the same in both CTAs
+    csync();  // every partial of this CTA is stored before the release
+    if (threadIdx.x == 0) {
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(fl + S.kh), "r"(tag) : "memory");
+        uint32_t ok = 1;
+        for (uint32_t i = 0;; ++i) {
+            if (ld_acquire(fl + (S.kh ^ 1u)) == tag) break;
+            if ((i & 63) == 63 && ld_volatile(&p.bar[1])) {
+                ok = 0;
+                break;
+            }
+            if (i > kBarLimit) {
+                atomicExch(&p.bar[1], 1u);
+                raise_device_error(DEVERR_FLAG_TIMEOUT);
+                ok = 0;
+                break;
+            }
+        }
+        flag[2] = ok;
+    }
+    csync();
+    c.ok = c.ok && flag[2] != 0;
+    if (!c.ok && threadIdx.x == 0) *c.B.abort = 1;
+    return c.ok;
+}
+
 // C: zero a slice of the QKV sums (read in B, next written in the next layer's
 // A), RMSNorm -> gate/up rows of FFN [f0, f0+U) -> SwiGLU -> down projection of
 // those U indices, added into Y.
@@ -1173,10 +1207,20 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, U = S.U;
     float *gu = reinterpret_cast<float *>(c.smem + c.L.gu);
     const uint32_t ngu = (2 * U + 127) / 128;  // gate/up tiles: rows [gate 0..U) [up 0..U)
-    for (uint32_t t = warp >> 2; t < ngu; t += kCW / 4) {
-        const float s = acc_row(c.tbase, 8 * t);
-        const uint32_t r = t * 128 + 32 * (warp & 3) + lane;
-        if (r < 2 * U) gu[r] = s;
+    if (S.ks > 1) {
+        // K-split pair: publish this CTA's partial sums, wait for the partner's, and
+        // add the two halves in K order (identical bits in both CTAs)
+        float *mine = p.ffx + ((size_t)(S.f0 / 64) * 2 + S.kh) * 128;
+        if (warp < 4) mine[32 * warp + lane] = acc_row(c.tbase, 0);
+        if (!ffn_pair_exchange(c, S)) return;
+        const float *h0 = p.ffx + (size_t)(S.f0 / 64) * 2 * 128, *h1 = h0 + 128;
+        for (uint32_t r = threadIdx.x; r < 2 * U; r += kCons) gu[r] = __ldcg(h0 + r) + __ldcg(h1 + r);
+    } else {
+        for (uint32_t t = warp >> 2; t < ngu; t += kCW / 4) {
+            const float s = acc_row(c.tbase, 8 * t);
+            const uint32_t r = t * 128 + 32 * (warp & 3) + lane;
+            if (r < 2 * U) gu[r] = s;
+        }
     }
     csync();
     float *h = reinterpret_cast<float *>(c.smem + c.L.xv);
@@ -1199,12 +1243,13 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     // the down MMAs are done) is read by the bulk copy before this thread reaches
     // the next grid barrier.
     float *stg = reinterpret_cast<float *>(c.smem + c.L.xv);
-    for (uint32_t t = warp >> 2; t < mt; t += kCW / 4)
+    const uint32_t ta = mt * S.kh / S.ks, tb = mt * (S.kh + 1) / S.ks;  // this CTA's down tiles
+    for (uint32_t t = ta + (warp >> 2); t < tb; t += kCW / 4)
         stg[t * 128 + 32 * (warp & 3) + lane] = acc_row(c.tbase, 8 * t);
     fence_proxy_async_smem();
     csync();
     if (threadIdx.x == 0) {
-        tc::bulk_reduce_add_f32(p.tp_size > 1 ? p.tpd : p.Y, stg, p.dim * 4);
+        tc::bulk_reduce_add_f32((p.tp_size > 1 ? p.tpd : p.Y) + ta * 128, stg + ta * 128, (tb - ta) * 128 * 4);
         tc::bulk_commit();
         tc::bulk_wait_all();
     }
@@ -1647,6 +1692,7 @@ struct Engine {
     Params p;
     int grid = 0;
     size_t smem = 0;
+    size_t bar_bytes = 16;  // cleared before every launch: barrier words and FFN split flags
     uint64_t arena_bytes = 0;
     std::vector<void *> allocs;
 };
@@ -1714,14 +1760,31 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
     if (c.dim % 128 || c.ffn % 32 || (hd != 64 && hd != 128) || c.n_heads % c.n_kv_heads || c.dim > 8192)
         PTC_UNSUPPORTED("tensor-core decode: unsupported shape");
     const uint32_t rows_qkv = qd + 2 * kvd, kb64 = c.dim / 64, otile = c.dim / 128;
-    // FFN slices: 32-index units, contiguous per CTA
+    // FFN slices: 32-index units, contiguous per CTA.  When every unit has a CTA of
+    // its own (ffn / 32 <= CTAs: the 8B shape at TP >= 4, small models), pairs of
+    // CTAs share 64-index units instead, each taking half of gate/up's K and half of
+    // down's output tiles: the same CTAs hold FFN work, but each one's gate/up MMA
+    // chain is K/128 instead of K/64 steps and its down chain half as long; the pair
+    // adds its partial gate/up sums (exchanged through global memory) before SwiGLU.
     const uint32_t nunits = c.ffn / 32;
     std::vector<Sched> S(G);
     for (auto &s : S) memset(&s, 0, sizeof(Sched));
+    const bool pairs = c.ffn % 64 == 0 && nunits <= (uint32_t)G && kb64 % 2 == 0 && otile % 2 == 0;
+    const uint32_t n64 = c.ffn / 64;
     uint32_t minU = ~0u;
+    if (pairs) {
+        for (uint32_t q = 0; q < 2 * n64; ++q) {
+            Sched &s = S[(uint64_t)q * G / (2 * n64)];
+            s.f0 = 64 * (q / 2), s.U = 64, s.ks = 2, s.kh = q % 2;
+        }
+    }
     for (int g = 0; g < G; ++g) {
-        const uint32_t u0 = (uint32_t)((uint64_t)nunits * g / G), u1 = (uint32_t)((uint64_t)nunits * (g + 1) / G);
-        S[g].f0 = 32 * u0, S[g].U = 32 * (u1 - u0);
+        if (!pairs) {
+            const uint32_t u0 = (uint32_t)((uint64_t)nunits * g / G), u1 = (uint32_t)((uint64_t)nunits * (g + 1) / G);
+            S[g].f0 = 32 * u0, S[g].U = 32 * (u1 - u0), S[g].ks = 1, S[g].kh = 0;
+        } else if (S[g].U == 0) {
+            S[g].ks = 1;
+        }
         if (S[g].U > 128) PTC_UNSUPPORTED("tensor-core decode: FFN slice of %u > 128 indices per CTA", S[g].U);
         minU = std::min(minU, S[g].U);
     }
@@ -1845,19 +1908,21 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
             }
             if (s.U) {  // C: gate/up tiles over the concatenation [gate | up], then down
                 const uint32_t ngu = (2 * s.U + 127) / 128;
+                const uint32_t kb0 = kb64 * s.kh / s.ks, kb1 = kb64 * (s.kh + 1) / s.ks;  // this CTA's K part
                 for (uint32_t q = 0; q < ngu; ++q) {
                     const uint32_t nrows = std::min(128u, 2 * s.U - 128 * q), r8 = (nrows + 7) / 8;
                     const uint32_t pc = per_chunk(0, r8);
-                    for (uint32_t b = 0; b < kb64; b += pc) {
-                        const uint32_t nb = std::min<uint32_t>(pc, kb64 - b);
-                        auto d = chunk(s, false, PH_GU, nb, 0, 255, b, q, b != 0, r8, rec);
+                    for (uint32_t b = kb0; b < kb1; b += pc) {
+                        const uint32_t nb = std::min<uint32_t>(pc, kb1 - b);
+                        auto d = chunk(s, false, PH_GU, nb, 0, 255, b, q, b != kb0, r8, rec);
                         job(in.gu[l], 2, s.f0, s.U, 128 * q, nrows, 2 * b, nb, 0, r8, 0, d);
                     }
                 }
                 const uint8_t km = (s.U % 64) ? 1 : 0;
                 const uint32_t bpa = km ? s.U / 32 : s.U / 64, per = std::max(1u, per_chunk(km, 16) / bpa);
-                for (uint32_t t0 = 0; t0 < otile; t0 += per) {
-                    const uint32_t nt = std::min(per, otile - t0);
+                const uint32_t ta = otile * s.kh / s.ks, tb = otile * (s.kh + 1) / s.ks;  // down tiles
+                for (uint32_t t0 = ta; t0 < tb; t0 += per) {
+                    const uint32_t nt = std::min(per, tb - t0);
                     auto d = chunk(s, false, PH_DOWN, nt * bpa, km, bpa, 0, t0, false, 16, rec);
                     for (uint32_t t = t0; t < t0 + nt; ++t)
                         job(in.down[l], 0, 0, 0, t * 128, 128, s.f0 / 32, bpa, km, 16, (t - t0) * bpa, d);
@@ -1934,7 +1999,9 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
     float *X = nullptr, *Y = nullptr, *qkv = nullptr, *cval = nullptr;
     rc = dalloc(e, &arena, off);
     if (!rc) rc = dalloc(e, &dsched, (size_t)G);
-    if (!rc) rc = dalloc(e, &bar, 4);
+    if (!rc) rc = dalloc(e, &bar, 4 + (pairs ? 2 * n64 : 0));
+    float *ffx = nullptr;
+    if (!rc && pairs) rc = dalloc(e, &ffx, (size_t)n64 * 2 * 128);
     if (tpin) {  // X, Y and the candidates live in the exchange area
         X = tpin->xr[tpin->rank], Y = tpin->yr[tpin->rank];
     } else {
@@ -1964,7 +2031,7 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
         err = cudaMemcpyAsync(djobs, jobs.data(), jobs.size() * sizeof(PackJob), cudaMemcpyHostToDevice, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(Y, 0, c.dim * 4, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(qkv, 0, rows_qkv * 4, st);
-    if (err == cudaSuccess) err = cudaMemsetAsync(bar, 0, 16, st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(bar, 0, (4 + (pairs ? 2 * n64 : 0)) * 4, st);
     for (size_t j0 = 0; j0 < jobs.size() && err == cudaSuccess; j0 += 65535) {
         const unsigned nj = (unsigned)std::min<size_t>(65535, jobs.size() - j0);
         pack_kernel<<<nj, 256, 0, st>>>(djobs + j0, arena);
@@ -1982,6 +2049,8 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
     P.embed = in.embed, P.cos_t = in.cos_t, P.sin_t = in.sin_t, P.kc = in.kc, P.vc = in.vc;
     P.X = X, P.Y = Y, P.qkv = qkv, P.logits = in.logits, P.cand_val = cval, P.cand_idx = cidx;
     P.attn_part = apart, P.attn_slices = slices;
+    P.ffx = ffx;
+    e->bar_bytes = (4 + (pairs ? 2 * n64 : 0)) * 4;
     P.tp_rank = 0, P.tp_size = 1, P.v0 = 0, P.epoch = nullptr;
     P.xr[0] = X, P.yr[0] = Y, P.cvr[0] = cval, P.cir[0] = cidx;
     if (tpin) {
@@ -2028,7 +2097,7 @@ extern "C" FP4X_API int fp4x_tc_mma_timestamps(unsigned long long *out, uint32_t
 
 int launch(Engine *e, cudaStream_t st, uint32_t n_tokens) {
     if (n_tokens == 0) return FP4X_OK;
-    cudaError_t err = cudaMemsetAsync(e->p.bar, 0, 16, st);
+    cudaError_t err = cudaMemsetAsync(e->p.bar, 0, e->bar_bytes, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->p.qkv, 0, (e->p.qd + 2 * e->p.kvd) * 4, st);
     if (err != cudaSuccess) return fail("reset", err);
     Params p = e->p;

@@ -64,6 +64,9 @@ struct Sched {
     uint32_t h0, nh;                                             // attended heads [h0, h0 + nh)
     uint32_t f0, U;                                              // FFN indices [f0, f0 + U)
     uint32_t n_l, l_tile[kMaxLm];                                // lm_head tiles
+    // FFN K split: ks CTAs share [f0, f0 + U), CTA part kh of them holding K range
+    // kh / ks of gate/up and down output tiles [kh mt / ks, (kh + 1) mt / ks)
+    uint32_t ks, kh;
     uint32_t pad;
     uint64_t stream_off;
     uint64_t layer_bytes, lm_bytes;
@@ -96,7 +99,8 @@ struct Params {
     const uint32_t *prompt;
     uint32_t *out;
     uint32_t n_tokens;
-    uint32_t *bar;  // [0] grid-barrier counter, [1] abort, [2] cross-rank release word
+    uint32_t *bar;  // [0] grid-barrier counter, [1] abort, [2] cross-rank release word, [4 ..): FFN split flags
+    float *ffx;     // FFN split partial gate/up sums [ffn / 64][2][128]
     // tensor parallelism (tp_size 1: xr[0] = X, yr[0] = Y, cvr[0] = cand_val, cir[0] = cand_idx)
     uint32_t tp_rank, tp_size, v0;             // this rank, ranks, first vocab row of the lm_head shard
     float *xr[kMaxTp], *yr[kMaxTp];            // every rank's X and Y (row-parallel outputs add into all)
