@@ -197,7 +197,26 @@ __global__ void __launch_bounds__(kThreads, PRO == PRO_NONE ? 5 : 1) gemv_kernel
     Prologue<PRO, XT> pro;
     pro.init(a);
     float ss = 0.0f;
-    {
+    if (PRO == PRO_NONE) {
+        // No norm: each warp stages exactly the 128-k groups its MMAs read below, so
+        // a warp barrier suffices and no warp waits for another's activation loads.
+        const uint32_t ngr = (nb + 3) / 4, s0 = (ngr * warp) / kWarps, s1 = (ngr * (warp + 1)) / kWarps;
+        constexpr int CH = 6;
+        for (uint32_t c0 = s0; c0 < s1; c0 += CH) {
+            float4 raw[CH];
+#pragma unroll
+            for (int u = 0; u < CH; ++u) {
+                const uint32_t c = c0 + u, b = 4 * c + (lane >> 3);
+                raw[u] = (c < s1 && b < nb) ? pro.raw4((size_t)c * 128 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < CH; ++u) {
+                const uint32_t c = c0 + u, b = 4 * c + (lane >> 3);
+                if (c < s1) split4(raw[u], c * 128 + lane * 4, b, lane, b < nb, xhi, xlo, xpost);  // warp-uniform
+            }
+        }
+        __syncwarp();
+    } else {
         // chunk = 128 consecutive elements = 4 blocks; lane owns 4 elements, 8 lanes a block
         const uint32_t nchunks = (nb + 3) / 4;
         constexpr int CH = 6;  // chunks in flight per warp (K <= 6144 in one batch)
@@ -226,11 +245,11 @@ __global__ void __launch_bounds__(kThreads, PRO == PRO_NONE ? 5 : 1) gemv_kernel
             }
         }
     }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
     float rms = 1.0f;  // RMSNorm's scalar is applied to the row results (W(x*w)*rms = W(x*rms*w))
     if (PRO != PRO_NONE) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
         float tot = 0.0f;
 #pragma unroll
         for (int i = 0; i < kWarps; ++i) tot += red[i];
@@ -301,19 +320,21 @@ __global__ void __launch_bounds__(kThreads, PRO == PRO_NONE ? 5 : 1) gemv_kernel
         part[warp * kRows + g + 8] = acc1;
     }
     __syncthreads();
+    float yv = 0.0f;  // row tid of the tile (tid < kRows)
     if (tid < kRows) {
         float s = part[tid];
 #pragma unroll
         for (int i = 1; i < kWarps; ++i) s += part[i * kRows + tid];
-        yt[tid] = s * rms;
+        yv = s * rms;
+        yt[tid] = yv;
     }
-    __syncthreads();
+    if (EPI != EPI_STORE && EPI != EPI_RESIDUAL) __syncthreads();  // these two write only their own row
 
     // 4) epilogue
     if (EPI == EPI_STORE) {
-        if (tid < (int)rows) a.y[row0 + tid] = yt[tid];
+        if (tid < (int)rows) a.y[row0 + tid] = yv;
     } else if (EPI == EPI_RESIDUAL) {
-        if (tid < (int)rows) a.y[row0 + tid] = a.y[row0 + tid] + yt[tid];  // llama_run:259
+        if (tid < (int)rows) a.y[row0 + tid] = a.y[row0 + tid] + yv;  // llama_run:259
     } else if (EPI == EPI_SWIGLU) {
         // tile rows 0..7 = gate[8*tile ..], rows 8..15 = up[8*tile ..]
         if (tid < 8) {
