@@ -228,7 +228,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 template <int HD>
 struct MmaCfg {
     static constexpr int kTile = 64;
-    static constexpr int kStages = HD == 64 ? 4 : 2;
+    // Two K/V stages at both head dims: at 64 dims the smaller ring fits about twice
+    // the CTAs per SM, which the slice model turns into more, shorter slices (B200,
+    // config 2: batch 1 / 8 at 32k 14.2 -> 13.1 / 55.7 -> 52.6 us, batch 64 at 2k / 8k
+    // 34.5 -> 29.6 / 97.0 -> 91.7 us; batch 64 at 512 positions 11.3 -> 13.1 us)
+    static constexpr int kStages = 2;
     static constexpr int kChunks = HD / 8;  // 16-byte pieces per row
     static constexpr size_t kStageElems = (size_t)kTile * HD;
     static constexpr size_t kSmem = (size_t)kStages * 2 * kStageElems * 2  // K and V ring
