@@ -1151,33 +1151,42 @@ __device__ void phase_attn_combine_o(Ctx &c, uint32_t lay_count) {
     o_projection(c, lay_count);
 }
 
-// The two CTAs of a K-split FFN pair meet: each has stored its partial gate/up sums
-// (this layer's) into its half of p.ffx; its flag word (cleared before every launch)
-// is released with the layer's barrier count, and the partner's is awaited
-// (bounded, abort-aware).  Uniform result over the CTA.
-__device__ bool ffn_pair_exchange(Ctx &c, const Sched &S) {
+// The two CTAs of a K-split FFN pair meet: row r's partial gate/up sum of each CTA
+// travels as one 64-bit word {tag, value} in its half of p.ffx, tag = (launch << 20)
+// | barrier count, so every word validates itself (no flag, no fence: the previous
+// use of a slot carries another tag).  Warps 0-3 (rows 0..127) store their word,
+// poll the partner's (bounded, abort-aware) and add the halves in K order into
+// gu (identical bits in both CTAs).  Uniform result over the CTA.
+__device__ bool ffn_pair_exchange(Ctx &c, const Sched &S, float *gu) {
     const Params &p = *c.p;
     volatile uint32_t *flag = reinterpret_cast<volatile uint32_t *>(c.smem + c.L.flag);
-    uint32_t *fl = p.bar + 4 + (S.f0 / 64) * 2;
-    const uint32_t tag = c.nbar;  // >= 1 here, the same in both CTAs
-    csync();  // every partial of this CTA is stored before the release
-    if (threadIdx.x == 0) {
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(fl + S.kh), "r"(tag) : "memory");
-        uint32_t ok = 1;
-        for (uint32_t i = 0;; ++i) {
-            if (ld_acquire(fl + (S.kh ^ 1u)) == tag) break;
-            if ((i & 63) == 63 && ld_volatile(&p.bar[1])) {
-                ok = 0;
-                break;
-            }
-            if (i > kBarLimit) {
-                atomicExch(&p.bar[1], 1u);
-                raise_device_error(DEVERR_FLAG_TIMEOUT);
-                ok = 0;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = 32 * warp + lane;
+    const uint32_t tag = (p.launch_seq << 20) | (c.nbar & 0xFFFFFu);
+    if (threadIdx.x == 0) flag[2] = 1;
+    csync();
+    if (warp < 4) {
+        const float own = acc_row(c.tbase, 0);
+        uint64_t *pair = p.ffx + (size_t)(S.f0 / 64) * 2 * 128;
+        const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(own);
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(pair + S.kh * 128 + r), "l"(w) : "memory");
+        const uint64_t *src = pair + (S.kh ^ 1u) * 128 + r;
+        uint64_t v = 0;
+        bool ok = true;
+        for (uint32_t it = 0;; ++it) {
+            asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
+            if ((uint32_t)(v >> 32) == tag) break;
+            if (((it & 63) == 63 && ld_volatile(&p.bar[1])) || it > kBarLimit) {
+                if (it > kBarLimit) {
+                    atomicExch(&p.bar[1], 1u);
+                    raise_device_error(DEVERR_FLAG_TIMEOUT);
+                }
+                ok = false;
                 break;
             }
         }
-        flag[2] = ok;
+        const float other = __uint_as_float((uint32_t)v);
+        if (ok && r < 2 * S.U) gu[r] = S.kh == 0 ? own + other : other + own;
+        if (!ok) flag[2] = 0;
     }
     csync();
     c.ok = c.ok && flag[2] != 0;
@@ -1210,11 +1219,7 @@ __device__ void phase_ffn(Ctx &c, uint32_t l, uint32_t lay_count) {
     if (S.ks > 1) {
         // K-split pair: publish this CTA's partial sums, wait for the partner's, and
         // add the two halves in K order (identical bits in both CTAs)
-        float *mine = p.ffx + ((size_t)(S.f0 / 64) * 2 + S.kh) * 128;
-        if (warp < 4) mine[32 * warp + lane] = acc_row(c.tbase, 0);
-        if (!ffn_pair_exchange(c, S)) return;
-        const float *h0 = p.ffx + (size_t)(S.f0 / 64) * 2 * 128, *h1 = h0 + 128;
-        for (uint32_t r = threadIdx.x; r < 2 * U; r += kCons) gu[r] = __ldcg(h0 + r) + __ldcg(h1 + r);
+        if (!ffn_pair_exchange(c, S, gu)) return;
     } else {
         for (uint32_t t = warp >> 2; t < ngu; t += kCW / 4) {
             const float s = acc_row(c.tbase, 8 * t);
@@ -1692,7 +1697,7 @@ struct Engine {
     Params p;
     int grid = 0;
     size_t smem = 0;
-    size_t bar_bytes = 16;  // cleared before every launch: barrier words and FFN split flags
+    uint32_t launches = 0;  // launches so far (the FFN split tags)
     uint64_t arena_bytes = 0;
     std::vector<void *> allocs;
 };
@@ -1999,8 +2004,8 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
     float *X = nullptr, *Y = nullptr, *qkv = nullptr, *cval = nullptr;
     rc = dalloc(e, &arena, off);
     if (!rc) rc = dalloc(e, &dsched, (size_t)G);
-    if (!rc) rc = dalloc(e, &bar, 4 + (pairs ? 2 * n64 : 0));
-    float *ffx = nullptr;
+    if (!rc) rc = dalloc(e, &bar, 4);
+    uint64_t *ffx = nullptr;
     if (!rc && pairs) rc = dalloc(e, &ffx, (size_t)n64 * 2 * 128);
     if (tpin) {  // X, Y and the candidates live in the exchange area
         X = tpin->xr[tpin->rank], Y = tpin->yr[tpin->rank];
@@ -2031,7 +2036,8 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
         err = cudaMemcpyAsync(djobs, jobs.data(), jobs.size() * sizeof(PackJob), cudaMemcpyHostToDevice, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(Y, 0, c.dim * 4, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(qkv, 0, rows_qkv * 4, st);
-    if (err == cudaSuccess) err = cudaMemsetAsync(bar, 0, (4 + (pairs ? 2 * n64 : 0)) * 4, st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(bar, 0, 16, st);
+    if (err == cudaSuccess && ffx) err = cudaMemsetAsync(ffx, 0, (size_t)n64 * 2 * 128 * 8, st);  // tag 0: never valid
     for (size_t j0 = 0; j0 < jobs.size() && err == cudaSuccess; j0 += 65535) {
         const unsigned nj = (unsigned)std::min<size_t>(65535, jobs.size() - j0);
         pack_kernel<<<nj, 256, 0, st>>>(djobs + j0, arena);
@@ -2049,8 +2055,7 @@ int build(const persist::BuildIn &in, cudaStream_t st, Engine **out, const TpIn 
     P.embed = in.embed, P.cos_t = in.cos_t, P.sin_t = in.sin_t, P.kc = in.kc, P.vc = in.vc;
     P.X = X, P.Y = Y, P.qkv = qkv, P.logits = in.logits, P.cand_val = cval, P.cand_idx = cidx;
     P.attn_part = apart, P.attn_slices = slices;
-    P.ffx = ffx;
-    e->bar_bytes = (4 + (pairs ? 2 * n64 : 0)) * 4;
+    P.ffx = ffx, P.launch_seq = 0;
     P.tp_rank = 0, P.tp_size = 1, P.v0 = 0, P.epoch = nullptr;
     P.xr[0] = X, P.yr[0] = Y, P.cvr[0] = cval, P.cir[0] = cidx;
     if (tpin) {
@@ -2097,11 +2102,12 @@ extern "C" FP4X_API int fp4x_tc_mma_timestamps(unsigned long long *out, uint32_t
 
 int launch(Engine *e, cudaStream_t st, uint32_t n_tokens) {
     if (n_tokens == 0) return FP4X_OK;
-    cudaError_t err = cudaMemsetAsync(e->p.bar, 0, e->bar_bytes, st);
+    cudaError_t err = cudaMemsetAsync(e->p.bar, 0, 16, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->p.qkv, 0, (e->p.qd + 2 * e->p.kvd) * 4, st);
     if (err != cudaSuccess) return fail("reset", err);
     Params p = e->p;
     p.n_tokens = n_tokens;
+    p.launch_seq = e->launches++ % 4095u + 1u;  // 1..4095: 12 bits above the FFN split tags' barrier count
     void *args[] = {&p};
     err = cudaLaunchCooperativeKernel((const void *)decode_tc_kernel, dim3(e->grid), dim3(kThreads), args, e->smem, st);
     if (err != cudaSuccess) return fail("cooperative launch", err);

@@ -99,8 +99,9 @@ struct Params {
     const uint32_t *prompt;
     uint32_t *out;
     uint32_t n_tokens;
-    uint32_t *bar;  // [0] grid-barrier counter, [1] abort, [2] cross-rank release word, [4 ..): FFN split flags
-    float *ffx;     // FFN split partial gate/up sums [ffn / 64][2][128]
+    uint32_t *bar;        // [0] grid-barrier counter, [1] abort, [2] cross-rank release word
+    uint64_t *ffx;        // FFN split partial gate/up sums [ffn / 64][2][128] as {tag, f32} words
+    uint32_t launch_seq;  // launches of this engine so far (this one included): FFN split tags
     // tensor parallelism (tp_size 1: xr[0] = X, yr[0] = Y, cvr[0] = cand_val, cir[0] = cand_idx)
     uint32_t tp_rank, tp_size, v0;             // this rank, ranks, first vocab row of the lm_head shard
     float *xr[kMaxTp], *yr[kMaxTp];            // every rank's X and Y (row-parallel outputs add into all)
